@@ -1,0 +1,421 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   D[M,N] = alpha * sum_k A(m,k) * B(n,k)      (fp32 accumulation in TMEM)
+//
+// Operand storage (row-major, leading dimension in elements):
+//   A K-major  : A[M,K]           A MN-major : At[K,M]
+//   B K-major  : B[N,K]           B MN-major : Bt[K,N]
+// which covers the three GEMMs of a linear layer without any transpose copy:
+//   forward  Y  = X  W^T   (A=X  K-major,  B=W  K-major)
+//   dgrad    dX = dY W     (A=dY K-major,  B=W  MN-major)
+//   wgrad    dW = dY^T X   (A=dY MN-major, B=X  MN-major)
+//
+// The reference computes these with library GEMMs behind F.linear
+// (parallel/tensor_parallel.py:57,79; model/transformer.py:46).  Here the
+// epilogue also fuses the element-wise work that follows each GEMM in the
+// model: GELU (fc1), GELU-backward (fc2 dgrad), residual add (attn.o / fc2),
+// and fp32 gradient accumulation into the flat main-grad buffer (wgrad).
+//
+// CTA = 6 warps: warp 0 issues TMA loads, warp 1 owns TMEM and issues
+// tcgen05.mma from one thread, warps 2-5 drain the accumulator (tcgen05.ld)
+// and run the epilogue.  Two TMEM accumulators let the epilogue of tile i
+// overlap the main loop of tile i+1.  Tiles are 128 x BN x 64.
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+namespace mmb {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;          // 32 KB / 16 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;             // double-buffered accumulator
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+};
+
+// Grouped rasterisation: walk GROUP_M m-tiles down each n column so the B
+// tile and a band of A tiles stay hot in L2.
+__device__ __forceinline__ void tile_coords(int t, int mtiles, int ntiles, int& tm, int& tn) {
+  constexpr int GROUP_M = 16;
+  const int per_group = GROUP_M * ntiles;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsz = min(mtiles - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  tm = first_m + r % gsz;
+  tn = r / gsz;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&r)[32]) {
+  const int nvalid = min(32, a.N - col0);  // multiple of 8 (host checks N % 8 == 0)
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * a.alpha;
+
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.D) + (size_t)row * a.ldd + col0;
+    __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(a.aux) + (size_t)row * a.ld_aux + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (8 * j < nvalid) {
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+        if constexpr (EPI == EPI_BF16) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ow[e] = pack_bf16x2(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+        } else if constexpr (EPI == EPI_GELU) {
+          uint4 pre;
+          uint32_t* pw = reinterpret_cast<uint32_t*>(&pre);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float x0 = v[8 * j + 2 * e], x1 = v[8 * j + 2 * e + 1];
+            pw[e] = pack_bf16x2(x0, x1);
+            ow[e] = pack_bf16x2(gelu_f(x0), gelu_f(x1));
+          }
+          *reinterpret_cast<uint4*>(aux + 8 * j) = pre;
+        } else {  // EPI_DGELU: out = acc * gelu'(pre)
+          const uint4 pre = *reinterpret_cast<const uint4*>(aux + 8 * j);
+          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&pre);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 p = unpack_bf16x2(pw[e]);
+            ow[e] = pack_bf16x2(v[8 * j + 2 * e] * gelu_grad_f(p.x), v[8 * j + 2 * e + 1] * gelu_grad_f(p.y));
+          }
+        }
+        *reinterpret_cast<uint4*>(out + 8 * j) = o;
+      }
+    }
+  } else {
+    float* out = reinterpret_cast<float*>(a.D) + (size_t)row * a.ldd + col0;
+    const float* res = a.resid + (size_t)row * a.ld_resid + col0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (4 * j < nvalid) {
+        float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if constexpr (EPI == EPI_F32_ACC) {
+          const float4 c = *reinterpret_cast<const float4*>(out + 4 * j);
+          o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+        } else if constexpr (EPI == EPI_RESID) {
+          const float4 c = *reinterpret_cast<const float4*>(res + 4 * j);
+          o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+        }
+        *reinterpret_cast<float4*>(out + 4 * j) = o;
+      }
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+  using C = GemmCfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int mtiles = (args.M + BM - 1) / BM;
+  const int ntiles = (args.N + BN - 1) / BN;
+  const int num_tiles = mtiles * ntiles;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, mtiles, ntiles, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrGemmEmptyWait, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          issued_mask |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          uint8_t* b_dst = sB + stage * C::B_BYTES;
+          const int k0 = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let loads already in flight land before the CTA (and its smem) goes
+        // away: stage s completes the phase with the parity it was issued in.
+        for (int s = 0; s < STAGES; ++s) {
+          if (!((issued_mask >> s) & 1u)) continue;
+          const uint32_t par = (issued_par >> s) & 1u;
+          const unsigned long long t0 = globaltimer();
+          while (!mbar_try_wait(&full[s], par) && globaltimer() - t0 < 10000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, args.err, kErrGemmAccEmptyWait, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmFullWait, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? make_sdesc_sw128(a_addr + k * 2048, 8192, 1024)
+                                        : make_sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_sdesc_sw128(b_addr + k * 2048, 8192, 1024)
+                                        : make_sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);   // accumulator ready for the epilogue
+      }
+      if (!ok) {
+        // Drain: wait (bounded) until every MMA issued so far has completed.
+        umma_commit(drain);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < 10000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      // One lane waits, the warp follows: tcgen05.ld below is warp-collective,
+      // so the whole warp must agree on whether to continue.
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, args.err, kErrGemmAccFullWait, abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, mtiles, ntiles, tm, tn);
+      const int row = tm * BM + q * 32 + lane;
+      const int n0 = tn * BN;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_wait_ld();
+        if (row < args.M && n0 + c < args.N) epilogue_chunk<EPI>(args, row, n0 + c, r);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ============================================================================ host side
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows, cols] with leading
+// dimension `ld` (elements), 128-byte swizzle, box {box_cols, box_rows}.
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols,
+                      int box_rows) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return -1;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return -2;
+  if ((ld * 2) % 16 != 0) return -3;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -4;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                              cudaStream_t stream) {
+  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI>;
+  constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
+  static bool attr_set = false;  // per instantiation
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, args);
+  return cudaGetLastError();
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                                cudaStream_t s) {
+  switch (args.epi) {
+    case EPI_BF16: return launch_one<BN, A_MN, B_MN, EPI_BF16>(ta, tb, args, grid, s);
+    case EPI_F32: return launch_one<BN, A_MN, B_MN, EPI_F32>(ta, tb, args, grid, s);
+    case EPI_F32_ACC: return launch_one<BN, A_MN, B_MN, EPI_F32_ACC>(ta, tb, args, grid, s);
+    case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU>(ta, tb, args, grid, s);
+    case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, args, grid, s);
+    case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, args, grid, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int BN>
+static cudaError_t dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, bool a_mn,
+                                  bool b_mn, int grid, cudaStream_t s) {
+  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false>(ta, tb, args, grid, s);
+  if (!a_mn && b_mn) return dispatch_epi<BN, false, true>(ta, tb, args, grid, s);
+  if (a_mn && b_mn) return dispatch_epi<BN, true, true>(ta, tb, args, grid, s);
+  return dispatch_epi<BN, true, false>(ta, tb, args, grid, s);
+}
+
+int choose_bn(int M, int N, int num_sms) {
+  if (N <= 128) return 128;
+  const long mt = (M + BM - 1) / BM;
+  const long t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
+  const double w256 = (double)((t256 + num_sms - 1) / num_sms) * 256.0;
+  const double w128 = (double)((t128 + num_sms - 1) / num_sms) * 128.0 * 1.15;  // lower intensity per column
+  return (w128 < w256) ? 128 : 256;
+}
+
+// Returns 0 on success, a negative host-side validation code, or a positive cudaError_t.
+int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return -10;
+  if (p.N % 8 != 0) return -11;
+  if ((reinterpret_cast<uintptr_t>(p.args.D) & 15) != 0) return -12;
+  const int bn = p.bn > 0 ? p.bn : choose_bn(p.M, p.N, p.num_sms);
+  CUtensorMap ta, tb;
+  int rc;
+  if (!p.a_mn) rc = make_tmap_bf16_2d(&ta, p.A, p.M, p.K, p.lda, 64, BM);
+  else rc = make_tmap_bf16_2d(&ta, p.A, p.K, p.M, p.lda, 64, 64);
+  if (rc) return rc - 20;
+  if (!p.b_mn) rc = make_tmap_bf16_2d(&tb, p.B, p.N, p.K, p.ldb, 64, bn);
+  else rc = make_tmap_bf16_2d(&tb, p.B, p.K, p.N, p.ldb, 64, 64);
+  if (rc) return rc - 30;
+  GemmArgs args = p.args;
+  args.M = p.M;
+  args.N = p.N;
+  args.K = p.K;
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn);
+  const int grid = std::min(tiles, p.num_sms > 0 ? p.num_sms : 148);
+  cudaError_t e = (bn == 256) ? dispatch_major<256>(ta, tb, args, p.a_mn, p.b_mn, grid, stream)
+                              : dispatch_major<128>(ta, tb, args, p.a_mn, p.b_mn, grid, stream);
+  return e == cudaSuccess ? 0 : (int)e;
+}
+
+}  // namespace mmb

@@ -1,0 +1,49 @@
+// Host-visible interface of the tcgen05 GEMM (no torch headers here so the
+// kernel translation units compile quickly and can be reused by plain C/C++).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace mmb {
+
+enum GemmEpilogue : int {
+  EPI_BF16 = 0,     // D(bf16)  = alpha*acc
+  EPI_F32 = 1,      // D(fp32)  = alpha*acc
+  EPI_F32_ACC = 2,  // D(fp32) += alpha*acc            (gradient accumulation)
+  EPI_GELU = 3,     // aux(bf16) = alpha*acc ; D(bf16) = gelu(alpha*acc)
+  EPI_RESID = 4,    // D(fp32)  = resid(fp32) + alpha*acc (resid may alias D)
+  EPI_DGELU = 5,    // D(bf16)  = alpha*acc * gelu'(aux(bf16))
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int epi;
+  void* D;
+  long ldd;
+  void* aux;
+  long ld_aux;
+  const float* resid;
+  long ld_resid;
+  float alpha;
+  int* err;  // device error word (bounded-wait timeouts)
+};
+
+struct GemmProblem {
+  const void* A;
+  long lda;
+  bool a_mn;
+  const void* B;
+  long ldb;
+  bool b_mn;
+  int M, N, K;
+  int bn;       // 0 = heuristic, else 128 / 256
+  int num_sms;  // persistent grid size cap
+  GemmArgs args;
+};
+
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols,
+                      int box_rows);
+int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream);
+int choose_bn(int M, int N, int num_sms);
+
+}  // namespace mmb

@@ -1,0 +1,112 @@
+"""Numerics of the tcgen05 GEMM against an fp32 PyTorch reference.
+
+Covers the three operand layouts a linear layer needs (forward, dgrad,
+wgrad), ragged M/N/K tails, both tile widths, and every fused epilogue.
+"""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from mini_megatron_b200 import _C
+    return _C
+
+
+def _operands(M, N, K, a_mn, b_mn, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    b = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    A = a.t().contiguous() if a_mn else a
+    B = b.t().contiguous() if b_mn else b
+    ref = a.float() @ b.float().t()
+    return A, B, ref
+
+
+def _check_close(out, ref, rtol):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= rtol * scale, f"max abs err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 384, 320), (300, 392, 200), (1024, 2304, 768)])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_layouts_fp32_out(a_mn, b_mn, M, N, K, bn):
+    C = _C()
+    if a_mn and M % 8:
+        pytest.skip("MN-major A needs M % 8 == 0 (TMA row stride)")
+    A, B, ref = _operands(M, N, K, a_mn, b_mn)
+    D = torch.full((M, N), float("nan"), device="cuda")
+    C.gemm(A, a_mn, B, b_mn, D, C.EPI_F32, bn=bn)
+    torch.cuda.synchronize()
+    assert C.get_error() == 0
+    _check_close(D, ref, 1e-3)
+
+
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_bf16_out_and_alpha(bn):
+    C = _C()
+    M, N, K = 512, 768, 768
+    A, B, ref = _operands(M, N, K, False, False, seed=1)
+    D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, False, B, False, D, C.EPI_BF16, alpha=0.5, bn=bn)
+    torch.cuda.synchronize()
+    _check_close(D, 0.5 * ref, 1e-2)
+
+
+def test_gemm_accumulate():
+    C = _C()
+    M, N, K = 384, 256, 512
+    A, B, ref = _operands(M, N, K, True, True, seed=2)
+    D = torch.randn(M, N, device="cuda")
+    D0 = D.clone()
+    C.gemm(A, True, B, True, D, C.EPI_F32_ACC)
+    torch.cuda.synchronize()
+    _check_close(D, D0 + ref, 1e-3)
+
+
+def test_gemm_gelu_and_dgelu():
+    C = _C()
+    M, N, K = 512, 1024, 256
+    A, B, ref = _operands(M, N, K, False, False, seed=3)
+    D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    pre = torch.empty_like(D)
+    C.gemm(A, False, B, False, D, C.EPI_GELU, aux=pre)
+    torch.cuda.synchronize()
+    _check_close(pre, ref, 1e-2)
+    _check_close(D, torch.nn.functional.gelu(ref), 1e-2)
+    # dgelu: out = acc * gelu'(pre)
+    D2 = torch.empty_like(D)
+    C.gemm(A, False, B, False, D2, C.EPI_DGELU, aux=pre)
+    torch.cuda.synchronize()
+    x = pre.float().requires_grad_(True)
+    torch.nn.functional.gelu(x).backward(torch.ones_like(x))
+    _check_close(D2, ref * x.grad, 2e-2)
+
+
+def test_gemm_residual_inplace():
+    C = _C()
+    M, N, K = 256, 768, 3072
+    A, B, ref = _operands(M, N, K, False, False, seed=4)
+    R = torch.randn(M, N, device="cuda")
+    expect = R + ref
+    C.gemm(A, False, B, False, R, C.EPI_RESID, resid=R)
+    torch.cuda.synchronize()
+    _check_close(R, expect, 1e-3)
+
+
+def test_gemm_strided_views():
+    """Operands that are column slices of a wider buffer (e.g. q/k/v of a fused qkv)."""
+    C = _C()
+    M, K = 256, 192
+    big = torch.randn(M, 3 * K, device="cuda").bfloat16()
+    a = big[:, K:2 * K]
+    b = torch.randn(320, K, device="cuda").bfloat16()
+    D = torch.empty(M, 320, device="cuda")
+    C.gemm(a, False, b, False, D, C.EPI_F32)
+    torch.cuda.synchronize()
+    _check_close(D, a.float() @ b.float().t(), 1e-3)
