@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cmath>
 #include <vector>
 
 #include "ops.h"
@@ -72,6 +73,7 @@ void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, Tensor& D, int
   p.K = (int)K;
   p.bn = (int)bn;
   p.num_sms = num_sms();
+  p.allow_split = true;
   p.args.epi = (int)epi;
   p.args.D = D.data_ptr();
   p.args.ldd = D.stride(0);
@@ -102,6 +104,147 @@ void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, Tensor& D, int
   TORCH_CHECK(rc == 0, "gemm launch failed, code ", rc);
 }
 
+#define MMB_CHECK_RC(rc, what) TORCH_CHECK((rc) == 0, what " failed, code ", (rc))
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void check_f32(const Tensor& t, const char* n) {
+  check_cuda(t, n);
+  TORCH_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous(), n, " must be contiguous fp32");
+}
+void check_bf16(const Tensor& t, const char* n) {
+  check_cuda(t, n);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.is_contiguous(), n, " must be contiguous bf16");
+}
+
+// ----------------------------------------------------------------- LayerNorm
+// x [rows, H] fp32 -> y bf16, mean/rstd fp32 [rows]
+void layernorm_fwd(const Tensor& x, const Tensor& gamma, const Tensor& beta, Tensor& y, Tensor& mean, Tensor& rstd,
+                   double eps) {
+  check_f32(x, "x");
+  check_f32(gamma, "gamma");
+  check_f32(beta, "beta");
+  check_bf16(y, "y");
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  const int rc = mmb::layernorm_fwd(x.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(),
+                                    reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), mean.data_ptr<float>(),
+                                    rstd.data_ptr<float>(), rows, H, (float)eps, cur_stream());
+  MMB_CHECK_RC(rc, "layernorm_fwd");
+}
+
+// dx = LN_bwd(dy) (+ dres); dgamma/dbeta accumulated (+=) into the given fp32 buffers.
+void layernorm_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd, const Tensor& gamma,
+                   const c10::optional<Tensor>& dres, Tensor& dx, Tensor& dgamma, Tensor& dbeta) {
+  check_bf16(dy, "dy");
+  check_f32(x, "x");
+  check_f32(dx, "dx");
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  const int nparts = mmb::layernorm_bwd_parts(rows, H, num_sms());
+  Tensor part = at::empty({nparts, 2 * H}, x.options());
+  const float* dr = nullptr;
+  if (dres.has_value()) {
+    check_f32(*dres, "dres");
+    dr = dres->data_ptr<float>();
+  }
+  const int rc = mmb::layernorm_bwd(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), x.data_ptr<float>(),
+                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), gamma.data_ptr<float>(), dr,
+                                    dx.data_ptr<float>(), part.data_ptr<float>(), dgamma.data_ptr<float>(),
+                                    dbeta.data_ptr<float>(), rows, H, nparts, cur_stream());
+  MMB_CHECK_RC(rc, "layernorm_bwd");
+}
+
+// ----------------------------------------------------------------- cross-entropy
+std::vector<Tensor> ce_fwd_stats(const Tensor& logits, const Tensor& labels, int64_t vocab_start, int64_t n_valid) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.scalar_type() == at::kBFloat16, "bad logits");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels must be int64");
+  const int rows = (int)logits.size(0);
+  auto opt = logits.options().dtype(at::kFloat);
+  Tensor mx = at::empty({rows}, opt), sm = at::empty({rows}, opt), tg = at::empty({rows}, opt);
+  const int rc = mmb::ce_fwd_stats(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+                                   labels.data_ptr<int64_t>(), vocab_start, (int)n_valid, rows, mx.data_ptr<float>(),
+                                   sm.data_ptr<float>(), tg.data_ptr<float>(), cur_stream());
+  MMB_CHECK_RC(rc, "ce_fwd_stats");
+  return {mx, sm, tg};
+}
+
+void ce_bwd(Tensor& logits, const Tensor& labels, int64_t vocab_start, int64_t n_valid, const Tensor& lse,
+            const Tensor& scale) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.scalar_type() == at::kBFloat16, "bad logits");
+  check_f32(lse, "lse");
+  check_f32(scale, "scale");
+  const int rc = mmb::ce_bwd(reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+                             (int)logits.size(1), labels.data_ptr<int64_t>(), vocab_start, (int)n_valid,
+                             (int)logits.size(0), lse.data_ptr<float>(), scale.data_ptr<float>(), cur_stream());
+  MMB_CHECK_RC(rc, "ce_bwd");
+}
+
+// ----------------------------------------------------------------- embedding
+void embedding_fwd(const Tensor& ids, const Tensor& wte, const c10::optional<Tensor>& wpe, Tensor& out, int64_t S,
+                   int64_t vstart, int64_t vend) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids must be int64");
+  check_f32(wte, "wte");
+  check_f32(out, "out");
+  const int H = (int)wte.size(1);
+  const float* p = nullptr;
+  if (wpe.has_value()) {
+    check_f32(*wpe, "wpe");
+    p = wpe->data_ptr<float>();
+  }
+  const int rc = mmb::embedding_fwd(ids.data_ptr<int64_t>(), wte.data_ptr<float>(), p, out.data_ptr<float>(),
+                                    (int)ids.numel(), H, (int)S, vstart, vend, cur_stream());
+  MMB_CHECK_RC(rc, "embedding_fwd");
+}
+
+void embedding_bwd(const Tensor& ids, const Tensor& dout, Tensor& dwte, const c10::optional<Tensor>& dwpe,
+                   int64_t B, int64_t S, int64_t vstart, int64_t vend) {
+  check_f32(dout, "dout");
+  check_f32(dwte, "dwte");
+  float* p = nullptr;
+  if (dwpe.has_value()) {
+    check_f32(*dwpe, "dwpe");
+    p = dwpe->data_ptr<float>();
+  }
+  const int rc = mmb::embedding_bwd(ids.data_ptr<int64_t>(), dout.data_ptr<float>(), dwte.data_ptr<float>(), p,
+                                    (int)B, (int)S, (int)dwte.size(1), vstart, vend, cur_stream());
+  MMB_CHECK_RC(rc, "embedding_bwd");
+}
+
+// ----------------------------------------------------------------- AdamW
+void adamw_flat(Tensor& p, const Tensor& g, Tensor& m, Tensor& v, const c10::optional<Tensor>& pb, double lr,
+                double b1, double b2, double eps, double wd, int64_t step, double grad_scale) {
+  check_f32(p, "p");
+  check_f32(g, "g");
+  check_f32(m, "m");
+  check_f32(v, "v");
+  TORCH_CHECK(p.numel() == g.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "adamw size mismatch");
+  __nv_bfloat16* pbp = nullptr;
+  if (pb.has_value()) {
+    check_bf16(*pb, "pb");
+    TORCH_CHECK(pb->numel() == p.numel(), "adamw bf16 shadow size mismatch");
+    pbp = reinterpret_cast<__nv_bfloat16*>(pb->data_ptr());
+  }
+  const double bc1 = 1.0 - std::pow(b1, (double)step);
+  const double bc2 = 1.0 - std::pow(b2, (double)step);
+  const int rc = mmb::adamw_flat(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                                 pbp, p.numel(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd,
+                                 (float)(lr / bc1), (float)std::sqrt(bc2), (float)grad_scale, num_sms(),
+                                 cur_stream());
+  MMB_CHECK_RC(rc, "adamw_flat");
+}
+
+void cast_f32_bf16(const Tensor& x, Tensor& y) {
+  check_f32(x, "x");
+  check_bf16(y, "y");
+  TORCH_CHECK(x.numel() == y.numel(), "cast size mismatch");
+  MMB_CHECK_RC(mmb::cast_f32_bf16(x.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), x.numel(),
+                                  num_sms(), cur_stream()),
+               "cast_f32_bf16");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -111,6 +254,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("D"), py::arg("epi"), py::arg("aux") = c10::nullopt,
         py::arg("resid") = c10::nullopt, py::arg("alpha") = 1.0, py::arg("bn") = 0);
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("ce_fwd_stats", &ce_fwd_stats);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("adamw_flat", &adamw_flat);
+  m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("num_sms", &num_sms);
+  m.attr("EPI_F32_ATOMIC") = (int)mmb::EPI_F32_ATOMIC;
   m.attr("EPI_BF16") = (int)mmb::EPI_BF16;
   m.attr("EPI_F32") = (int)mmb::EPI_F32;
   m.attr("EPI_F32_ACC") = (int)mmb::EPI_F32_ACC;

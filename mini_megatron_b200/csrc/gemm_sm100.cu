@@ -103,7 +103,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int c
     for (int j = 0; j < 8; ++j) {
       if (4 * j < nvalid) {
         float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        if constexpr (EPI == EPI_F32_ACC) {
+        if constexpr (EPI == EPI_F32_ATOMIC) {
+          atomicAdd(reinterpret_cast<float4*>(out + 4 * j), o);  // split-K partial sums
+          continue;
+        } else if constexpr (EPI == EPI_F32_ACC) {
           const float4 c = *reinterpret_cast<const float4*>(out + 4 * j);
           o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
         } else if constexpr (EPI == EPI_RESID) {
@@ -165,8 +168,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int mtiles = (args.M + BM - 1) / BM;
   const int ntiles = (args.N + BN - 1) / BN;
-  const int num_tiles = mtiles * ntiles;
-  const int kblocks = (args.K + BK - 1) / BK;
+  const int kblocks_total = (args.K + BK - 1) / BK;
+  // Work unit = (output tile, K split).  Splits > 1 only with the atomic epilogue.
+  const int splits = args.splits > 0 ? args.splits : 1;
+  const int kb_per_split = (kblocks_total + splits - 1) / splits;
+  const int num_tiles = mtiles * ntiles * splits;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -177,9 +183,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t, mtiles, ntiles, tm, tn);
+        tile_coords(t / splits, mtiles, ntiles, tm, tn);
         const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb_lo = (t % splits) * kb_per_split;
+        const int kb_hi = min(kblocks_total, kb_lo + kb_per_split);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrGemmEmptyWait, abort_flag)) {
             ok = false;
             break;
@@ -237,7 +245,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb_lo = (t % splits) * kb_per_split;
+        const int kb_hi = min(kblocks_total, kb_lo + kb_per_split);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[stage], phase, args.err, kErrGemmFullWait, abort_flag)) {
             ok = false;
             break;
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                         : make_sdesc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_sdesc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : make_sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
           if (++stage == STAGES) {
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t, mtiles, ntiles, tm, tn);
+      tile_coords(t / splits, mtiles, ntiles, tm, tn);
       const int row = tm * BM + q * 32 + lane;
       const int n0 = tn * BN;
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
@@ -371,6 +381,7 @@ static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, co
     case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU>(ta, tb, args, grid, s);
     case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, args, grid, s);
     case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, args, grid, s);
+    case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC>(ta, tb, args, grid, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -393,12 +404,55 @@ int choose_bn(int M, int N, int num_sms) {
   return (w128 < w256) ? 128 : 256;
 }
 
+// Pick (tile width, K splits) for GEMMs whose output tiles cannot fill the
+// machine (weight gradients: small M x N, long K).  Cost model in units of
+// one 128x256x64 k-block: per wave, the longest unit's k-blocks plus a fixed
+// epilogue charge; narrower tiles cost 15% more per column.
+static void choose_split(int M, int N, int K, int num_sms, int& bn, int& splits) {
+  const int kblocks = (K + BK - 1) / BK;
+  double best = 1e30;
+  for (int b : {256, 128}) {
+    if (b == 256 && N <= 128) continue;
+    const long tiles = (long)((M + BM - 1) / BM) * ((N + b - 1) / b);
+    for (int sp = 1; sp <= 32; ++sp) {
+      if (sp > 1 && kblocks / sp < 4) break;
+      const int kps = (kblocks + sp - 1) / sp;
+      const int real_sp = (kblocks + kps - 1) / kps;
+      const long units = tiles * real_sp;
+      const long waves = (units + num_sms - 1) / num_sms;
+      const double per_unit = (b / 256.0) * (b == 128 ? 1.15 : 1.0) * (kps + (real_sp > 1 ? 4.0 : 2.0));
+      const double cost = waves * per_unit;
+      if (cost < best - 1e-9) {
+        best = cost;
+        bn = b;
+        splits = real_sp;
+      }
+    }
+  }
+}
+
 // Returns 0 on success, a negative host-side validation code, or a positive cudaError_t.
 int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return -10;
   if (p.N % 8 != 0) return -11;
   if ((reinterpret_cast<uintptr_t>(p.args.D) & 15) != 0) return -12;
-  const int bn = p.bn > 0 ? p.bn : choose_bn(p.M, p.N, p.num_sms);
+  const int sms = p.num_sms > 0 ? p.num_sms : 148;
+  GemmArgs args = p.args;
+  args.M = p.M;
+  args.N = p.N;
+  args.K = p.K;
+  args.splits = 1;
+  int bn = p.bn > 0 ? p.bn : choose_bn(p.M, p.N, sms);
+  const bool can_split = (args.epi == EPI_F32_ACC || args.epi == EPI_F32_ATOMIC) && p.allow_split;
+  if (can_split) {
+    int sbn = bn, sp = 1;
+    choose_split(p.M, p.N, p.K, sms, sbn, sp);
+    if (p.bn <= 0) bn = sbn;
+    if (sp > 1) {
+      args.splits = sp;
+      args.epi = EPI_F32_ATOMIC;
+    }
+  }
   CUtensorMap ta, tb;
   int rc;
   if (!p.a_mn) rc = make_tmap_bf16_2d(&ta, p.A, p.M, p.K, p.lda, 64, BM);
@@ -407,12 +461,8 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   if (!p.b_mn) rc = make_tmap_bf16_2d(&tb, p.B, p.N, p.K, p.ldb, 64, bn);
   else rc = make_tmap_bf16_2d(&tb, p.B, p.K, p.N, p.ldb, 64, 64);
   if (rc) return rc - 30;
-  GemmArgs args = p.args;
-  args.M = p.M;
-  args.N = p.N;
-  args.K = p.K;
-  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn);
-  const int grid = std::min(tiles, p.num_sms > 0 ? p.num_sms : 148);
+  const long units = (long)((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn) * args.splits;
+  const int grid = (int)std::min<long>(units, sms);
   cudaError_t e = (bn == 256) ? dispatch_major<256>(ta, tb, args, p.a_mn, p.b_mn, grid, stream)
                               : dispatch_major<128>(ta, tb, args, p.a_mn, p.b_mn, grid, stream);
   return e == cudaSuccess ? 0 : (int)e;

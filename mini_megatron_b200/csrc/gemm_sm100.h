@@ -13,6 +13,7 @@ enum GemmEpilogue : int {
   EPI_GELU = 3,     // aux(bf16) = alpha*acc ; D(bf16) = gelu(alpha*acc)
   EPI_RESID = 4,    // D(fp32)  = resid(fp32) + alpha*acc (resid may alias D)
   EPI_DGELU = 5,    // D(bf16)  = alpha*acc * gelu'(aux(bf16))
+  EPI_F32_ATOMIC = 6,  // D(fp32) += alpha*acc with atomics (split-K partial sums)
 };
 
 struct GemmArgs {
@@ -25,7 +26,8 @@ struct GemmArgs {
   const float* resid;
   long ld_resid;
   float alpha;
-  int* err;  // device error word (bounded-wait timeouts)
+  int* err;     // device error word (bounded-wait timeouts)
+  int splits;   // K splits (set by the launcher)
 };
 
 struct GemmProblem {
@@ -38,6 +40,7 @@ struct GemmProblem {
   int M, N, K;
   int bn;       // 0 = heuristic, else 128 / 256
   int num_sms;  // persistent grid size cap
+  bool allow_split;  // accumulate epilogues may split K across CTAs (atomics)
   GemmArgs args;
 };
 

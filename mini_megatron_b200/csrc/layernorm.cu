@@ -1,0 +1,222 @@
+// LayerNorm forward / backward for sm_100a.
+//
+// Forward : y(bf16) = (x - mean) * rstd * gamma + beta, x fp32 (the fp32
+//           residual stream), statistics in fp32; mean/rstd saved for backward.
+//           The bf16 output feeds the next GEMM directly (the reference
+//           runs nn.LayerNorm in fp32 under autocast and then casts to bf16
+//           at every F.linear: model/transformer.py:54-61).
+// Backward: dx(fp32) = rstd * (g*dy - mean(g*dy) - xhat*mean(g*dy*xhat))
+//           [+ dres: the residual-stream gradient is added in the same pass]
+//           dgamma/dbeta: per-warp partial sums (fused into the row pass for
+//           H <= 1024, a separate column pass above that), folded by a last
+//           kernel that accumulates into the fp32 main-grad buffers.
+//
+// One warp per row; a row is held in registers as float4 (H/128 per lane) so
+// x is read exactly once per pass.
+#include <algorithm>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace mmb {
+
+template <int NV>  // float4 per lane
+__global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                     const float* __restrict__ beta, __nv_bfloat16* __restrict__ y,
+                                                     float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                     int rows, int H, float eps) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nvec = H >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * H);
+  float4 v[NV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    v[i] = (c < nvec) ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
+  }
+  const float mean = warp_sum(s) / H;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
+      ss += a * a + b * b + cc * cc + d * d;
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(ss) / H + eps);
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  uint2* yr = reinterpret_cast<uint2*>(y + (size_t)row * H);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      const float4 g = g4[c], b = b4[c];
+      uint2 o;
+      o.x = pack_bf16x2((v[i].x - mean) * rstd * g.x + b.x, (v[i].y - mean) * rstd * g.y + b.y);
+      o.y = pack_bf16x2((v[i].z - mean) * rstd * g.z + b.z, (v[i].w - mean) * rstd * g.w + b.w);
+      yr[c] = o;
+    }
+  }
+  if (lane == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+}
+
+// Row pass.  With FUSE_PARAM, each warp also accumulates dgamma/dbeta over the
+// rows it visits and writes them to part[global_warp][0:2H].
+template <int NV, bool FUSE_PARAM>
+__global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
+                                                     const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                     const float* __restrict__ gamma, const float* __restrict__ dres,
+                                                     float* __restrict__ dx, float* __restrict__ part, int rows,
+                                                     int H) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  const int nvec = H >> 2;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  float4 dg[FUSE_PARAM ? NV : 1], db[FUSE_PARAM ? NV : 1];
+  if constexpr (FUSE_PARAM) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) dg[i] = db[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int r = gw; r < rows; r += nwarps) {
+    const float mu = mean[r], rs = rstd[r];
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * H);
+    const uint2* dyr = reinterpret_cast<const uint2*>(dy + (size_t)r * H);
+    float4 xh[NV], gdy[NV];
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        const float4 xv = xr[c];
+        const float4 g = g4[c];
+        const uint2 du = dyr[c];
+        const float2 d01 = unpack_bf16x2(du.x), d23 = unpack_bf16x2(du.y);
+        xh[i] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
+        gdy[i] = make_float4(d01.x * g.x, d01.y * g.y, d23.x * g.z, d23.y * g.w);
+        a += gdy[i].x + gdy[i].y + gdy[i].z + gdy[i].w;
+        b += gdy[i].x * xh[i].x + gdy[i].y * xh[i].y + gdy[i].z * xh[i].z + gdy[i].w * xh[i].w;
+        if constexpr (FUSE_PARAM) {
+          dg[i].x += d01.x * xh[i].x; dg[i].y += d01.y * xh[i].y; dg[i].z += d23.x * xh[i].z; dg[i].w += d23.y * xh[i].w;
+          db[i].x += d01.x; db[i].y += d01.y; db[i].z += d23.x; db[i].w += d23.y;
+        }
+      }
+    }
+    a = warp_sum(a) / H;
+    b = warp_sum(b) / H;
+    float4* dxr = reinterpret_cast<float4*>(dx + (size_t)r * H);
+    const float4* drr = dres ? reinterpret_cast<const float4*>(dres + (size_t)r * H) : nullptr;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        float4 o = make_float4(rs * (gdy[i].x - a - xh[i].x * b), rs * (gdy[i].y - a - xh[i].y * b),
+                               rs * (gdy[i].z - a - xh[i].z * b), rs * (gdy[i].w - a - xh[i].w * b));
+        if (drr) {
+          const float4 d = drr[c];
+          o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
+        }
+        dxr[c] = o;
+      }
+    }
+  }
+  if constexpr (FUSE_PARAM) {
+    float4* pg = reinterpret_cast<float4*>(part + (size_t)gw * 2 * H);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        pg[c] = dg[i];
+        pg[nvec + c] = db[i];
+      }
+    }
+  }
+}
+
+// Column pass for wide rows: CTA (band, column block of 256 columns); each
+// thread owns one column and walks the band's rows.
+__global__ void __launch_bounds__(256) ln_param_part_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                            const float* __restrict__ x, const float* __restrict__ mean,
+                                                            const float* __restrict__ rstd, float* __restrict__ part,
+                                                            int rows, int H, int rows_per_band) {
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  const int r0 = blockIdx.x * rows_per_band, r1 = min(rows, r0 + rows_per_band);
+  float g = 0.f, b = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const float d = __bfloat162float(dy[(size_t)r * H + c]);
+    g += d * (x[(size_t)r * H + c] - mean[r]) * rstd[r];
+    b += d;
+  }
+  part[(size_t)blockIdx.x * 2 * H + c] = g;
+  part[(size_t)blockIdx.x * 2 * H + H + c] = b;
+}
+
+// main_grad[gamma] += sum_p part[p][0:H]; main_grad[beta] += sum_p part[p][H:2H]
+__global__ void ln_param_grad_kernel(const float* __restrict__ part, int nparts, int H, float* __restrict__ dgamma,
+                                     float* __restrict__ dbeta) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 2 * H) return;
+  float acc = 0.f;
+  for (int p = 0; p < nparts; ++p) acc += part[(size_t)p * 2 * H + c];
+  if (c < H) dgamma[c] += acc;
+  else dbeta[c - H] += acc;
+}
+
+int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bfloat16* y, float* mean, float* rstd,
+                  int rows, int H, float eps, cudaStream_t s) {
+  if (H % 4 != 0 || H > 4096) return -1;
+  const int threads = 256;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  const int nv = (H / 4 + 31) / 32;
+#define LN_FWD(NVV) ln_fwd_kernel<NVV><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, H, eps)
+  if (nv <= 2) LN_FWD(2);
+  else if (nv <= 6) LN_FWD(6);
+  else if (nv <= 8) LN_FWD(8);
+  else if (nv <= 16) LN_FWD(16);
+  else LN_FWD(32);
+#undef LN_FWD
+  return (int)cudaGetLastError();
+}
+
+// Number of fp32 [2H] partial rows the backward needs as scratch.
+int layernorm_bwd_parts(int rows, int H, int num_sms) {
+  const int nv = (H / 4 + 31) / 32;
+  if (nv <= 8) return 8 * std::min(2 * num_sms, std::max(1, (rows + 7) / 8));  // one per warp
+  return std::min(4 * num_sms, std::max(1, rows / 16));                          // one per band
+}
+
+int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
+                  const float* dres, float* dx, float* part, float* dgamma, float* dbeta, int rows, int H,
+                  int nparts, cudaStream_t s) {
+  if (H % 4 != 0 || H > 4096) return -1;
+  const int nv = (H / 4 + 31) / 32;
+  if (nv <= 8) {
+    const int blocks = nparts / 8;
+#define LN_BWD(NVV) ln_bwd_kernel<NVV, true><<<blocks, 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, part, rows, H)
+    if (nv <= 2) LN_BWD(2);
+    else if (nv <= 6) LN_BWD(6);
+    else LN_BWD(8);
+#undef LN_BWD
+  } else {
+    const int blocks = std::max(1, (rows * 32 + 255) / 256);
+    if (nv <= 16) ln_bwd_kernel<16, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, rows, H);
+    else ln_bwd_kernel<32, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, rows, H);
+    const int rows_per_band = (rows + nparts - 1) / nparts;
+    dim3 grid(nparts, (H + 255) / 256);
+    ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);
+  }
+  ln_param_grad_kernel<<<(2 * H + 255) / 256, 256, 0, s>>>(part, nparts, H, dgamma, dbeta);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace mmb

@@ -1,3 +1,33 @@
-// Declarations of every kernel launcher exported by the extension.
+// Declarations of every kernel launcher exported by the extension.  Launchers
+// return 0 on success, a negative code for a host-side validation failure, or
+// a positive cudaError_t.
 #pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
 #include "gemm_sm100.h"
+
+namespace mmb {
+
+int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bfloat16* y, float* mean, float* rstd,
+                  int rows, int H, float eps, cudaStream_t s);
+int layernorm_bwd_parts(int rows, int H, int num_sms);
+int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
+                  const float* dres, float* dx, float* part, float* dgamma, float* dbeta, int rows, int H,
+                  int nparts, cudaStream_t s);
+
+int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
+                 float* out_max, float* out_sum, float* out_tgt, cudaStream_t s);
+int ce_bwd(__nv_bfloat16* logits, long ld, int n_cols, const long* labels, long vocab_start, int n_valid, int rows,
+           const float* lse, const float* scale, cudaStream_t s);
+
+int embedding_fwd(const long* ids, const float* wte, const float* wpe, float* out, int rows, int H, int S,
+                  long vstart, long vend, cudaStream_t s);
+int embedding_bwd(const long* ids, const float* dout, float* dwte, float* dwpe, int B, int S, int H, long vstart,
+                  long vend, cudaStream_t s);
+
+int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, long n, float lr, float b1, float b2,
+               float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s);
+int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStream_t s);
+
+}  // namespace mmb

@@ -1,0 +1,206 @@
+"""Training engine: one object that owns topology, model chunk, optimizer, schedule.
+
+``Trainer(cfg).train_step(tokens, labels)`` runs ONE optimizer step:
+``num_microbatches`` forward/backward passes (through the 1F1B pipeline when
+pp > 1), the data-parallel gradient reduction (bucketed and overlapped with
+the last microbatch's backward), the sequence-parallel LayerNorm gradient
+reduction, then AdamW (flat, fused; or ZeRO-1 sharded) and the LR schedule.
+
+It is the framework's public training API; ``main.py`` (reference-compatible
+CLI) and ``bench.py`` are thin drivers around it.  The pieces it composes are
+usable on their own (see the package ``__init__``).
+
+Data: ``tokens``/``labels`` are ``[num_microbatches, B, S]`` int64 tensors (host
+or device; host tensors should be pinned and are copied asynchronously).
+Every rank passes the same batch for its data-parallel replica; stages that
+do not need tokens or labels ignore them.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+import os
+
+import torch
+import torch.distributed as dist
+
+from .config import GPTConfig
+from .models.gpt import GPTStage, build_gpt
+from .optim import FusedAdamW, make_param_buffer
+from .parallel import process_groups as pg
+from .parallel.data_parallel import GradSync, allreduce_sequence_parallel_grads
+from .parallel.distributed_optimizer import DistributedOptimizer
+from .parallel.pipeline_parallel import PipelineEngine
+
+
+def make_lr_lambda(warmup_steps, num_steps):
+    """Linear warm-up then cosine decay to 0 over ``num_steps`` total (reference main.py:36-43)."""
+    def get_lr(step):
+        if step < warmup_steps:
+            return step / max(warmup_steps, 1)
+        progress = (step - warmup_steps) / max(num_steps - warmup_steps, 1)
+        return 0.5 * (1.0 + math.cos(progress * math.pi))
+    return get_lr
+
+
+def compute_mfu(model, seq_len, micro_batch_size, tp, pp, elapsed, num_steps, peak_flops=None):
+    """Reference MFU formula (main.py:46-66) with the peak as a parameter (B200 dense bf16 by default)."""
+    L, h, V = model["num_layers"], model["hidden_size"], model["vocab_size"]
+    B, s = micro_batch_size, seq_len
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    dp_w = max(1, ws // (tp * pp))
+    gpu_world = tp * pp * dp_w
+    token_linear = (24 * h * h + 48 * h * h) * L + 6 * h * V
+    core_attn = 6 * h * L * B
+    flops_per_step = token_linear * B * s + core_attn * s * s
+    peak = peak_flops if peak_flops is not None else 2.25e15
+    return min(flops_per_step * num_steps * dp_w / (elapsed * peak * gpu_world), 1.0)
+
+
+@dataclasses.dataclass
+class TrainConfig:
+    model: GPTConfig = dataclasses.field(default_factory=GPTConfig)
+    micro_batch_size: int = 4
+    seq_len: int | None = None          # default: model.max_seq_len
+    num_microbatches: int = 1
+    tp: int = 1
+    pp: int = 1
+    sequence_parallel: bool = False
+    zero1: bool = False
+    schedule: str = "1f1b"
+    lr: float = 6e-4
+    weight_decay: float = 0.1
+    betas: tuple = (0.9, 0.999)
+    eps: float = 1e-8
+    warmup_steps: int = 10
+    num_steps: int = 100
+    dp_overlap: bool = True
+    bucket_mb: float = 64.0
+    recompute: bool = False
+    average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
+    seed: int = 42
+
+
+class Trainer:
+    def __init__(self, cfg: TrainConfig, device=None, mpu=None):
+        self.cfg = cfg
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else \
+                torch.device("cpu")
+        self.device = torch.device(device)
+        if not dist.is_initialized():
+            raise RuntimeError("torch.distributed must be initialised (world size 1 is fine)")
+        self.mpu = mpu or pg.init_model_parallel(cfg.tp, cfg.pp, cfg.sequence_parallel)
+        pg.set_model_parallel(self.mpu)
+        mpu = self.mpu
+        self.seq_len = cfg.seq_len or cfg.model.max_seq_len
+        if self.seq_len > cfg.model.max_seq_len:
+            raise ValueError("seq_len exceeds the position table")
+        sp = self.mpu["sequence_parallel"]
+        if sp and self.seq_len % cfg.tp:
+            raise ValueError("sequence parallelism needs seq_len % tp == 0")
+        # identical init on every rank of a TP group and every DP replica (same seed),
+        # distinct per pipeline stage only through construction order
+        torch.manual_seed(cfg.seed)
+        if cfg.pp > 1:
+            self.model = GPTStage(cfg.model, mpu["pp_rank"], cfg.pp, recompute=cfg.recompute)
+        else:
+            self.model = build_gpt(cfg.model, recompute=cfg.recompute)
+        self.model.to(self.device)
+        dp = mpu["dp_size"]
+        bucket_elems = int(cfg.bucket_mb * (1 << 20) / 4)
+        self.buf = make_param_buffer(self.model, align=dp, bucket_elems=bucket_elems)
+        grad_scale = 1.0 / dp
+        if cfg.zero1:
+            self.optimizer = DistributedOptimizer(self.buf, mpu["dp_group"], lr=cfg.lr, betas=cfg.betas,
+                                                  eps=cfg.eps, weight_decay=cfg.weight_decay,
+                                                  overlap=cfg.dp_overlap)
+            self.grad_sync = self.optimizer.grad_sync
+        else:
+            self.optimizer = FusedAdamW(self.model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                        weight_decay=cfg.weight_decay, grad_scale=grad_scale)
+            self.grad_sync = GradSync(self.buf, mpu["dp_group"], mode="allreduce", overlap=cfg.dp_overlap)
+        layers = self.model.decoder_layers if cfg.pp > 1 else self.model.decoder.layers
+        self.grad_sync.attach(list(layers))
+        self.scheduler = torch.optim.lr_scheduler.LambdaLR(self.optimizer,
+                                                           make_lr_lambda(cfg.warmup_steps, cfg.num_steps))
+        self.sp_params = [p for p in self.model.parameters() if getattr(p, "sequence_parallel_grad", False)]
+        S_local = self.seq_len // cfg.tp if sp else self.seq_len
+        self.engine = None
+        if cfg.pp > 1:
+            prev, nxt = pg.pp_peers()
+            self.engine = PipelineEngine(self.model, mpu["pp_rank"], cfg.pp, prev, nxt,
+                                         (cfg.micro_batch_size, S_local, cfg.model.hidden_size), self.device,
+                                         schedule=cfg.schedule)
+        self.step_count = 0
+        # a collective on the default group before the first (batched) p2p
+        if dist.get_world_size() > 1:
+            t = torch.zeros(1, device=self.device)
+            dist.all_reduce(t)
+
+    # ------------------------------------------------------------------ step
+    def _loss_mask(self):
+        return torch.ones(self.cfg.micro_batch_size, self.seq_len, dtype=torch.float32, device=self.device)
+
+    def train_step(self, tokens, labels, loss_mask=None):
+        """One optimizer step over ``tokens/labels [m, B, S]``; returns the mean loss tensor (last stage) or None."""
+        cfg = self.cfg
+        m = cfg.num_microbatches
+        if tokens.dim() == 2:
+            tokens, labels = tokens.unsqueeze(0), labels.unsqueeze(0)
+        tokens = tokens.to(self.device, non_blocking=True)
+        labels = labels.to(self.device, non_blocking=True)
+        mask = self._loss_mask() if loss_mask is None else loss_mask.to(self.device, non_blocking=True)
+        scale = 1.0 / m if cfg.average_microbatches else 1.0
+        self.optimizer.zero_grad()
+        self.grad_sync.reset()
+        if self.engine is None:
+            total = None
+            for mb in range(m):
+                if mb == m - 1:
+                    self.grad_sync.overlap = cfg.dp_overlap
+                else:
+                    self.grad_sync.overlap = False
+                _, loss = self.model(tokens[mb], labels[mb], mask if mask.dim() == 2 else mask[mb])
+                (loss * scale).backward()
+                total = loss.detach() if total is None else total + loss.detach()
+            result = total / m
+        else:
+            def batch_fn(mb):
+                return tokens[mb], labels[mb], (mask if mask.dim() == 2 else mask[mb])
+
+            def pre_backward(mb):
+                # only the last microbatch's backward may launch DP buckets
+                self.grad_sync.overlap = cfg.dp_overlap if mb == m - 1 else False
+
+            losses = self.engine.run(batch_fn, m, loss_scale=scale, pre_backward=pre_backward)
+            result = torch.stack([l.detach() for l in losses]).mean() if losses else None
+        self.grad_sync.overlap = cfg.dp_overlap
+        if not cfg.zero1:
+            self.grad_sync.finish()
+        if self.sp_params:
+            allreduce_sequence_parallel_grads(self.sp_params, self.mpu["tp_group"])
+        self.optimizer.step()
+        self.scheduler.step()
+        self.step_count += 1
+        return result
+
+    # ------------------------------------------------------------------ utils
+    def state_for_checkpoint(self):
+        return self.model, self.optimizer, self.scheduler
+
+    def destroy(self):
+        pg.set_model_parallel(None)
+
+
+def synthetic_batch(num_microbatches, B, S, vocab, seed=0, pin=False, shift=True):
+    """Uniform-random tokens with next-token-shift labels (last label = -100)."""
+    g = torch.Generator().manual_seed(seed)
+    toks = torch.randint(0, vocab, (num_microbatches, B, S + (1 if shift else 0)), generator=g)
+    if shift:
+        tokens, labels = toks[..., :-1].contiguous(), toks[..., 1:].contiguous()
+    else:
+        tokens, labels = toks, toks.clone()
+    if pin and torch.cuda.is_available():
+        tokens, labels = tokens.pin_memory(), labels.pin_memory()
+    return tokens, labels

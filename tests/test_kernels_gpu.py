@@ -1,0 +1,116 @@
+"""Numerics of the memory-bound sm_100a kernels against fp32 PyTorch references."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _C():
+    from mini_megatron_b200 import _C
+    return _C
+
+
+@pytest.mark.parametrize("H", [64, 768, 1024, 2048, 4096])
+def test_layernorm_fwd_bwd(H):
+    C = _C()
+    torch.manual_seed(0)
+    rows = 1000
+    x = torch.randn(rows, H, device="cuda") * 3 + 1
+    g = torch.randn(H, device="cuda")
+    b = torch.randn(H, device="cuda")
+    y = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)
+    mean = torch.empty(rows, device="cuda")
+    rstd = torch.empty(rows, device="cuda")
+    C.layernorm_fwd(x, g, b, y, mean, rstd, 1e-5)
+    xr = x.clone().requires_grad_(True)
+    gr = g.clone().requires_grad_(True)
+    br = b.clone().requires_grad_(True)
+    ref = torch.nn.functional.layer_norm(xr, (H,), gr, br, 1e-5)
+    assert (y.float() - ref).abs().max().item() < 0.05 * ref.abs().max().item()
+    dy = torch.randn(rows, H, device="cuda").bfloat16()
+    dres = torch.randn(rows, H, device="cuda")
+    ref.backward(dy.float())
+    dx = torch.empty_like(x)
+    dg = torch.ones(H, device="cuda")   # accumulate on top of existing grads
+    db = torch.ones(H, device="cuda")
+    C.layernorm_bwd(dy, x, mean, rstd, g, dres, dx, dg, db)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(dx, xr.grad + dres, rtol=2e-3, atol=2e-3)
+    torch.testing.assert_close(dg, gr.grad + 1, rtol=2e-3, atol=2e-2)
+    torch.testing.assert_close(db, br.grad + 1, rtol=2e-3, atol=2e-2)
+
+
+@pytest.mark.parametrize("V,n_valid,start", [(50304, 50257, 0), (1024, 1024, 0), (6288, 6000, 6288)])
+def test_cross_entropy_stats_and_grad(V, n_valid, start):
+    C = _C()
+    torch.manual_seed(1)
+    rows = 300
+    logits = (torch.randn(rows, V, device="cuda") * 4).bfloat16()
+    labels = torch.randint(start, start + n_valid, (rows,), device="cuda")
+    labels[::7] = start + n_valid + 5 if start > 0 else labels[::7]   # some labels outside this shard
+    mx, se, tg = C.ce_fwd_stats(logits, labels, start, n_valid)
+    lf = logits.float()[:, :n_valid]
+    rmx = lf.max(-1).values
+    torch.testing.assert_close(mx, rmx)
+    torch.testing.assert_close(se, torch.exp(lf - rmx[:, None]).sum(-1), rtol=1e-4, atol=1e-4)
+    local = labels - start
+    inside = (local >= 0) & (local < n_valid)
+    rtg = torch.where(inside, lf.gather(1, local.clamp(0, n_valid - 1)[:, None])[:, 0], torch.zeros_like(rmx))
+    torch.testing.assert_close(tg, rtg)
+    lse = (rmx + torch.log(se)).contiguous()
+    scale = torch.rand(rows, device="cuda")
+    g = logits.clone()
+    C.ce_bwd(g, labels, start, n_valid, lse, scale)
+    p = torch.softmax(lf, -1)
+    onehot = torch.zeros_like(p)
+    onehot[inside, local[inside]] = 1
+    ref = torch.zeros(rows, V, device="cuda")
+    ref[:, :n_valid] = (p - onehot) * scale[:, None]
+    assert (g.float() - ref).abs().max().item() < 1e-2
+
+
+def test_embedding_fwd_bwd():
+    C = _C()
+    torch.manual_seed(2)
+    B, S, H, V = 4, 64, 768, 5000
+    ids = torch.randint(0, V, (B, S), device="cuda")
+    wte = torch.randn(V, H, device="cuda")
+    wpe = torch.randn(S, H, device="cuda")
+    out = torch.empty(B * S, H, device="cuda")
+    C.embedding_fwd(ids.view(-1), wte, wpe, out, S, 0, V)
+    ref = wte[ids] + wpe[None]
+    torch.testing.assert_close(out.view(B, S, H), ref)
+    # vocab shard [1000, 3000)
+    wsh = wte[1000:3000].contiguous()
+    out2 = torch.empty_like(out)
+    C.embedding_fwd(ids.view(-1), wsh, None, out2, S, 1000, 3000)
+    inside = (ids >= 1000) & (ids < 3000)
+    ref2 = torch.where(inside[..., None], wte[ids], torch.zeros_like(ref))
+    torch.testing.assert_close(out2.view(B, S, H), ref2)
+    dout = torch.randn(B * S, H, device="cuda")
+    dwte = torch.zeros(V, H, device="cuda")
+    dwpe = torch.zeros(S, H, device="cuda")
+    C.embedding_bwd(ids.view(-1), dout, dwte, dwpe, B, S, 0, V)
+    rwte = torch.zeros(V, H, device="cuda").index_add_(0, ids.view(-1), dout)
+    torch.testing.assert_close(dwte, rwte, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(dwpe, dout.view(B, S, H).sum(0), rtol=1e-4, atol=1e-4)
+
+
+def test_adamw_matches_torch():
+    C = _C()
+    torch.manual_seed(3)
+    n = 100_003
+    p = torch.randn(n, device="cuda")
+    ref = p.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([ref], lr=1e-3, weight_decay=0.1, foreach=False)
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    pb = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    for step in range(1, 4):
+        g = torch.randn(n, device="cuda")
+        ref.grad = g.clone()
+        opt.step()
+        C.adamw_flat(p, g * 2.0, m, v, pb, 1e-3, 0.9, 0.999, 1e-8, 0.1, step, 0.5)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(p, ref.detach(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(pb.float(), p.bfloat16().float())
