@@ -245,6 +245,45 @@ void cast_f32_bf16(const Tensor& x, Tensor& y) {
                "cast_f32_bf16");
 }
 
+// ----------------------------------------------------------------- attention
+// qkv [B*S, 3*nh*d] bf16 (columns [Q heads | K heads | V heads]) -> (out [B*S, nh*d] bf16, lse [B, nh, S] fp32)
+std::vector<Tensor> flash_attn_fwd(const Tensor& qkv, int64_t B, int64_t S, int64_t nh, int64_t d) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D bf16");
+  TORCH_CHECK(qkv.size(0) == B * S && qkv.size(1) == 3 * nh * d, "qkv shape mismatch");
+  TORCH_CHECK(S % 128 == 0, "flash attention needs S % 128 == 0");
+  TORCH_CHECK(d == 64 || d == 128, "flash attention supports head_dim 64 and 128");
+  Tensor out = at::empty({B * S, nh * d}, qkv.options());
+  Tensor lse = at::empty({B, nh, S}, qkv.options().dtype(at::kFloat));
+  const int rc = mmb::flash_attn_fwd(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), (int)B,
+                                     (int)S, (int)nh, (int)d, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                     out.stride(0), lse.data_ptr<float>(), (float)(1.0 / std::sqrt((double)d)),
+                                     error_word(), cur_stream());
+  MMB_CHECK_RC(rc, "flash_attn_fwd");
+  return {out, lse};
+}
+
+Tensor flash_attn_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse, int64_t B,
+                      int64_t S, int64_t nh, int64_t d) {
+  check_bf16(dout, "dout");
+  check_bf16(out, "out");
+  check_f32(lse, "lse");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D bf16");
+  TORCH_CHECK(dout.numel() == B * S * nh * d && out.numel() == B * S * nh * d, "attention bwd shape mismatch");
+  TORCH_CHECK(S % 128 == 0 && (d == 64 || d == 128), "unsupported attention shape");
+  Tensor dqkv = at::empty({B * S, 3 * nh * d}, qkv.options());
+  Tensor delta = at::empty({B, nh, S}, lse.options());
+  Tensor dq_acc = at::empty({B * S, nh * d}, lse.options());
+  const int rc = mmb::flash_attn_bwd(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), nh * d,
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), delta.data_ptr<float>(),
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dqkv.stride(0), (int)B, (int)S,
+      (int)nh, (int)d, (float)(1.0 / std::sqrt((double)d)), error_word(), num_sms(), cur_stream());
+  MMB_CHECK_RC(rc, "flash_attn_bwd");
+  return dqkv;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -263,6 +302,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_flat", &adamw_flat);
   m.def("cast_f32_bf16", &cast_f32_bf16);
   m.def("num_sms", &num_sms);
+  m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
   m.attr("EPI_F32_ATOMIC") = (int)mmb::EPI_F32_ATOMIC;
   m.attr("EPI_BF16") = (int)mmb::EPI_BF16;
   m.attr("EPI_F32") = (int)mmb::EPI_F32;

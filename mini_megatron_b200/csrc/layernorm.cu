@@ -162,14 +162,19 @@ __global__ void __launch_bounds__(256) ln_param_part_kernel(const __nv_bfloat16*
 }
 
 // main_grad[gamma] += sum_p part[p][0:H]; main_grad[beta] += sum_p part[p][H:2H]
+// Grid (column blocks, row groups): each CTA folds a slice of the partial rows
+// for 256 columns and adds it to the main grads with one atomic per column.
+constexpr int kLnFoldGroups = 32;
 __global__ void ln_param_grad_kernel(const float* __restrict__ part, int nparts, int H, float* __restrict__ dgamma,
                                      float* __restrict__ dbeta) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= 2 * H) return;
+  const int per = (nparts + gridDim.y - 1) / gridDim.y;
+  const int p0 = blockIdx.y * per, p1 = min(nparts, p0 + per);
+  if (p0 >= p1) return;
   float acc = 0.f;
-  for (int p = 0; p < nparts; ++p) acc += part[(size_t)p * 2 * H + c];
-  if (c < H) dgamma[c] += acc;
-  else dbeta[c - H] += acc;
+  for (int p = p0; p < p1; ++p) acc += part[(size_t)p * 2 * H + c];
+  atomicAdd(c < H ? &dgamma[c] : &dbeta[c - H], acc);
 }
 
 int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bfloat16* y, float* mean, float* rstd,
@@ -215,7 +220,8 @@ int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, co
     dim3 grid(nparts, (H + 255) / 256);
     ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);
   }
-  ln_param_grad_kernel<<<(2 * H + 255) / 256, 256, 0, s>>>(part, nparts, H, dgamma, dbeta);
+  dim3 fold((2 * H + 255) / 256, std::min(kLnFoldGroups, nparts));
+  ln_param_grad_kernel<<<fold, 256, 0, s>>>(part, nparts, H, dgamma, dbeta);
   return (int)cudaGetLastError();
 }
 

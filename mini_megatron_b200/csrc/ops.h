@@ -30,4 +30,11 @@ int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, 
                float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s);
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStream_t s);
 
+int flash_attn_fwd(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, int nh, int d, __nv_bfloat16* out,
+                   long ld_out, float* lse, float softmax_scale, int* err, cudaStream_t stream);
+int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* qkv, long ld_qkv,
+                   const __nv_bfloat16* out, const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv,
+                   long ld_dqkv, int B, int S, int nh, int d, float softmax_scale, int* err, int num_sms,
+                   cudaStream_t stream);
+
 }  // namespace mmb
