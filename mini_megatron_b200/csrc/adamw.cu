@@ -90,3 +90,21 @@ int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStr
 }
 
 }  // namespace mmb
+
+namespace mmb {
+
+// y = gelu(x), g = gelu'(x) in fp32 (the epilogue math, exposed for accuracy checks)
+__global__ void gelu_fwd_bwd_kernel(const float* __restrict__ x, float* __restrict__ y, float* __restrict__ g, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    y[i] = gelu_f(x[i]);
+    g[i] = gelu_grad_f(x[i]);
+  }
+}
+
+int gelu_fwd_bwd_f32(const float* x, float* y, float* g, long n, int num_sms, cudaStream_t s) {
+  const int blocks = (int)std::min<long>((n + 255) / 256, (long)num_sms * 8);
+  gelu_fwd_bwd_kernel<<<std::max(blocks, 1), 256, 0, s>>>(x, y, g, n);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace mmb

@@ -236,6 +236,15 @@ void adamw_flat(Tensor& p, const Tensor& g, Tensor& m, Tensor& v, const c10::opt
   MMB_CHECK_RC(rc, "adamw_flat");
 }
 
+std::vector<Tensor> gelu_fwd_bwd_f32(const Tensor& x) {
+  check_f32(x, "x");
+  Tensor y = at::empty_like(x), g = at::empty_like(x);
+  MMB_CHECK_RC(mmb::gelu_fwd_bwd_f32(x.data_ptr<float>(), y.data_ptr<float>(), g.data_ptr<float>(), x.numel(),
+                                     num_sms(), cur_stream()),
+               "gelu_fwd_bwd_f32");
+  return {y, g};
+}
+
 void cast_f32_bf16(const Tensor& x, Tensor& y) {
   check_f32(x, "x");
   check_bf16(y, "y");
@@ -284,6 +293,77 @@ Tensor flash_attn_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, 
   return dqkv;
 }
 
+// ----------------------------------------------------------------- symmetric memory
+int64_t symm_alloc(int64_t bytes) {
+  void* p = nullptr;
+  MMB_CHECK_RC(mmb::symm_alloc((size_t)bytes, &p), "symm_alloc");
+  return reinterpret_cast<int64_t>(p);
+}
+void symm_free(int64_t ptr) { MMB_CHECK_RC(mmb::symm_free(reinterpret_cast<void*>(ptr)), "symm_free"); }
+py::bytes symm_export(int64_t ptr) {
+  unsigned char h[64];
+  MMB_CHECK_RC(mmb::symm_export(reinterpret_cast<void*>(ptr), h), "symm_export");
+  return py::bytes(reinterpret_cast<const char*>(h), 64);
+}
+int64_t symm_open(py::bytes handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == 64, "IPC handle must be 64 bytes");
+  void* p = nullptr;
+  MMB_CHECK_RC(mmb::symm_open(reinterpret_cast<const unsigned char*>(s.data()), &p), "symm_open");
+  return reinterpret_cast<int64_t>(p);
+}
+void symm_close(int64_t ptr) { MMB_CHECK_RC(mmb::symm_close(reinterpret_cast<void*>(ptr)), "symm_close"); }
+
+// A tensor view of device memory owned elsewhere (the caller keeps it alive).
+Tensor tensor_from_ptr(int64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device) {
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel}, [](void*) {},
+                          at::TensorOptions().dtype(dtype).device(at::kCUDA, device));
+}
+
+// ----------------------------------------------------------------- fused DP step
+void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t>& grad,
+                    const std::vector<int64_t>& pbf16, const std::vector<int64_t>& sig, int64_t rank, int64_t bucket,
+                    int64_t epoch, int64_t lo, int64_t hi, Tensor& exp_avg, Tensor& exp_avg_sq, Tensor& counter,
+                    double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
+                    int64_t max_ctas) {
+  const int world = (int)param.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && grad.size() == param.size() && pbf16.size() == param.size() &&
+                  sig.size() == param.size(),
+              "fused DP needs 1..8 ranks");
+  check_f32(exp_avg, "exp_avg");
+  check_f32(exp_avg_sq, "exp_avg_sq");
+  TORCH_CHECK(exp_avg.numel() >= hi - lo && exp_avg_sq.numel() >= hi - lo, "moment buffers too small");
+  mmb::DpPeersHost P{};
+  P.world = world;
+  P.rank = (int)rank;
+  for (int r = 0; r < world; ++r) {
+    P.param[r] = reinterpret_cast<void*>(param[r]);
+    P.grad[r] = reinterpret_cast<void*>(grad[r]);
+    P.pbf16[r] = reinterpret_cast<void*>(pbf16[r]);
+    P.sig[r] = reinterpret_cast<void*>(sig[r]);
+  }
+  const double bc1 = 1.0 - std::pow(b1, (double)step), bc2 = 1.0 - std::pow(b2, (double)step);
+  mmb::DpStepHost s{};
+  s.bucket = (int)bucket;
+  s.epoch = (int)epoch;
+  s.lo = lo;
+  s.hi = hi;
+  s.exp_avg = exp_avg.data_ptr<float>();
+  s.exp_avg_sq = exp_avg_sq.data_ptr<float>();
+  s.lr = (float)lr;
+  s.b1 = (float)b1;
+  s.b2 = (float)b2;
+  s.eps = (float)eps;
+  s.wd = (float)wd;
+  s.step_size = (float)(lr / bc1);
+  s.bc2_sqrt = (float)std::sqrt(bc2);
+  s.grad_scale = (float)grad_scale;
+  s.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
+  s.err = error_word();
+  s.max_ctas = (int)max_ctas;
+  MMB_CHECK_RC(mmb::dp_rs_adamw_ag(P, s, cur_stream()), "dp_rs_adamw_ag");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -301,6 +381,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd", &embedding_bwd);
   m.def("adamw_flat", &adamw_flat);
   m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("gelu_fwd_bwd_f32", &gelu_fwd_bwd_f32);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_free", &symm_free);
+  m.def("symm_export", &symm_export);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("dp_rs_adamw_ag", &dp_rs_adamw_ag);
+  m.def("dp_signal_pad_bytes", &mmb::dp_signal_pad_bytes);
   m.def("num_sms", &num_sms);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);

@@ -68,10 +68,6 @@ __device__ __forceinline__ float exp2_approx(float x) {
   return y;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // Warp-uniform bounded wait: lane 0 polls, the result is broadcast.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           volatile int* abort_flag) {

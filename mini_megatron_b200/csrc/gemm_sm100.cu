@@ -31,7 +31,8 @@ namespace mmb {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;  // 2 producer/MMA warps + 8 epilogue warps
+constexpr int kEpiWarps = 8;
 
 template <int BN>
 struct GemmCfg {
@@ -40,7 +41,7 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;          // 32 KB / 16 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;             // double-buffered accumulator
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 8 * 4096 /*epilogue*/ + 256;  // one 4 KB stage per epilogue warp
 };
 
 // Grouped rasterisation: walk GROUP_M m-tiles down each n column so the B
@@ -56,72 +57,36 @@ __device__ __forceinline__ void tile_coords(int t, int mtiles, int ntiles, int& 
   tn = r / gsz;
 }
 
-template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int row, int col0, const uint32_t (&r)[32]) {
-  const int nvalid = min(32, a.N - col0);  // multiple of 8 (host checks N % 8 == 0)
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * a.alpha;
+// ---------------------------------------------------------------- epilogue helpers
+// Each epilogue warp owns 32 accumulator rows (one per lane).  A chunk of its
+// rows is staged in shared memory as 32 rows x 128 bytes in the TMA 128-byte
+// swizzle (16-byte unit u of row r lives at unit u ^ (r % 8)), then written by
+// ONE bulk tensor store (or reduce-add) issued by lane 0.
+constexpr int kStageBytes = 32 * 128;
 
-  if constexpr (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU) {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.D) + (size_t)row * a.ldd + col0;
-    __nv_bfloat16* aux = reinterpret_cast<__nv_bfloat16*>(a.aux) + (size_t)row * a.ld_aux + col0;
+__device__ __forceinline__ uint8_t* stage_unit(uint8_t* stg, int row, int unit) {
+  return stg + row * 128 + ((unit ^ (row & 7)) << 4);
+}
+
+// Cooperative, coalesced copy of a 32-row x 128-byte window of a row-major
+// global matrix into the swizzled stage (8 lanes per row, 4 rows per step).
+// Rows >= rows_valid or bytes past col_bytes_valid are skipped.
+__device__ __forceinline__ void stage_load(uint8_t* stg, const uint8_t* gbase, long ld_bytes, int rows_valid,
+                                           int col_bytes_valid, int lane) {
+  const int unit = lane & 7;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (8 * j < nvalid) {
-        uint4 o;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-        if constexpr (EPI == EPI_BF16) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) ow[e] = pack_bf16x2(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
-        } else if constexpr (EPI == EPI_GELU) {
-          uint4 pre;
-          uint32_t* pw = reinterpret_cast<uint32_t*>(&pre);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float x0 = v[8 * j + 2 * e], x1 = v[8 * j + 2 * e + 1];
-            pw[e] = pack_bf16x2(x0, x1);
-            ow[e] = pack_bf16x2(gelu_f(x0), gelu_f(x1));
-          }
-          *reinterpret_cast<uint4*>(aux + 8 * j) = pre;
-        } else {  // EPI_DGELU: out = acc * gelu'(pre)
-          const uint4 pre = *reinterpret_cast<const uint4*>(aux + 8 * j);
-          const uint32_t* pw = reinterpret_cast<const uint32_t*>(&pre);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 p = unpack_bf16x2(pw[e]);
-            ow[e] = pack_bf16x2(v[8 * j + 2 * e] * gelu_grad_f(p.x), v[8 * j + 2 * e + 1] * gelu_grad_f(p.y));
-          }
-        }
-        *reinterpret_cast<uint4*>(out + 8 * j) = o;
-      }
-    }
-  } else {
-    float* out = reinterpret_cast<float*>(a.D) + (size_t)row * a.ldd + col0;
-    const float* res = a.resid + (size_t)row * a.ld_resid + col0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (4 * j < nvalid) {
-        float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        if constexpr (EPI == EPI_F32_ATOMIC) {
-          atomicAdd(reinterpret_cast<float4*>(out + 4 * j), o);  // split-K partial sums
-          continue;
-        } else if constexpr (EPI == EPI_F32_ACC) {
-          const float4 c = *reinterpret_cast<const float4*>(out + 4 * j);
-          o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
-        } else if constexpr (EPI == EPI_RESID) {
-          const float4 c = *reinterpret_cast<const float4*>(res + 4 * j);
-          o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
-        }
-        *reinterpret_cast<float4*>(out + 4 * j) = o;
-      }
-    }
+  for (int it = 0; it < 8; ++it) {
+    const int row = it * 4 + (lane >> 3);
+    if (row < rows_valid && unit * 16 < col_bytes_valid)
+      *reinterpret_cast<uint4*>(stage_unit(stg, row, unit)) =
+          *reinterpret_cast<const uint4*>(gbase + (size_t)row * ld_bytes + unit * 16);
   }
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmAux,
                     const GemmArgs args) {
   using C = GemmCfg<BN>;
   constexpr int STAGES = C::STAGES;
@@ -130,7 +95,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * C::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t* sStage = smem + STAGES * C::STAGE_BYTES;  // 8 epilogue warps x 4 KB staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 8 * kStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
@@ -149,13 +115,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmD);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -281,8 +248,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    // bf16 outputs go out in 64-column chunks, fp32 outputs in 32-column
+    // chunks (128 bytes per row either way).  Warps w and w+4 share a TMEM lane
+    // quarter and take alternate chunks, so two warps per scheduler run the
+    // epilogue math.
+    constexpr bool OUT_BF16 = (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU);
+    constexpr int W = OUT_BF16 ? 64 : 32;
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // which alternate chunks this warp takes
+    uint8_t* stg = sStage + (warp - 2) * kStageBytes;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -296,19 +271,123 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       int tm, tn;
       tile_coords(t / splits, mtiles, ntiles, tm, tn);
-      const int row = tm * BM + q * 32 + lane;
+      const int r0 = tm * BM + q * 32;                 // first row of this warp
       const int n0 = tn * BN;
+      const int rows_valid = min(32, args.M - r0);
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+      const int nchunks = BN / W;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_wait_ld();
-        if (row < args.M && n0 + c < args.N) epilogue_chunk<EPI>(args, row, n0 + c, r);
+      for (int ch = half; ch < nchunks; ch += 2) {
+        const int col0 = n0 + ch * W;
+        if (col0 >= args.N) break;  // warp-uniform
+        float v[W];
+        {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + ch * W, r);
+          if constexpr (W == 64) {
+            uint32_t r2[32];
+            tmem_ld_32x32b_x32(t_row + ch * W + 32, r2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              v[i] = __uint_as_float(r[i]) * args.alpha;
+              v[32 + i] = __uint_as_float(r2[i]) * args.alpha;
+            }
+          } else {
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+          }
+        }
+        if (rows_valid <= 0) continue;
+        const int colb_valid = (args.N - col0) * (OUT_BF16 ? 2 : 4);
+        // the previous store from this warp's stage must have finished reading it
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+        if constexpr (EPI == EPI_BF16) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
+                make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                           pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+        } else if constexpr (EPI == EPI_GELU) {
+          // stage <- pre-activation, store it (aux); then stage <- gelu, stored below (D)
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float* x = v + 8 * u;
+            *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
+                make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                           pack_bf16x2(x[6], x[7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmAux, stg, col0, r0);
+            bulk_commit();
+          }
+#pragma unroll
+          for (int i = 0; i < W; ++i) v[i] = gelu_f(v[i]);
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float* x = v + 8 * u;
+            *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
+                make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
+                           pack_bf16x2(x[6], x[7]));
+          }
+        } else if constexpr (EPI == EPI_DGELU) {
+          // stage <- pre-activation tile (coalesced), then out = acc * gelu'(pre) in place
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(args.aux) + ((size_t)r0 * args.ld_aux + col0) * 2;
+          stage_load(stg, src, args.ld_aux * 2, rows_valid, colb_valid, lane);
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            uint4* pu = reinterpret_cast<uint4*>(stage_unit(stg, lane, u));
+            uint4 pre = *pu;
+            const uint32_t* pw = reinterpret_cast<const uint32_t*>(&pre);
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 pf = unpack_bf16x2(pw[e]);
+              o[e] = pack_bf16x2(v[8 * u + 2 * e] * gelu_grad_f(pf.x), v[8 * u + 2 * e + 1] * gelu_grad_f(pf.y));
+            }
+            *pu = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        } else if constexpr (EPI == EPI_RESID) {
+          // stage <- residual tile (coalesced), then out = resid + acc in place
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(args.resid) + ((size_t)r0 * args.ld_resid + col0) * 4;
+          stage_load(stg, src, args.ld_resid * 4, rows_valid, colb_valid, lane);
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            float4* pu = reinterpret_cast<float4*>(stage_unit(stg, lane, u));
+            float4 c = *pu;
+            c.x += v[4 * u]; c.y += v[4 * u + 1]; c.z += v[4 * u + 2]; c.w += v[4 * u + 3];
+            *pu = c;
+          }
+        } else {  // EPI_F32, EPI_F32_ACC, EPI_F32_ATOMIC
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(stage_unit(stg, lane, u)) =
+                make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (EPI == EPI_F32_ACC || EPI == EPI_F32_ATOMIC) {
+            tma_reduce_add_2d(&tmD, stg, col0, r0);
+          } else {
+            tma_store_2d(&tmD, stg, col0, r0);
+          }
+          bulk_commit();
+        }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -338,27 +417,31 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map over a row-major matrix [rows, cols] with leading
-// dimension `ld` (elements), 128-byte swizzle, box {box_cols, box_rows}.
-int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols,
-                      int box_rows) {
+// 2-D tensor map over a row-major matrix [rows, cols] with leading dimension
+// `ld` (elements), 128-byte swizzle, box {box_cols, box_rows}.
+static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, long rows, long cols,
+                        long ld, int box_cols, int box_rows) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return -1;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return -2;
-  if ((ld * 2) % 16 != 0) return -3;
+  if ((ld * esize) % 16 != 0) return -3;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -4;
 }
 
+int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols,
+                      int box_rows) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_cols, box_rows);
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
-static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
-                              cudaStream_t stream) {
+static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                              const CUtensorMap& tx, const GemmArgs& args, int grid, cudaStream_t stream) {
   auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI>;
   constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
   static bool attr_set = false;  // per instantiation
@@ -367,32 +450,33 @@ static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, cons
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, args);
+  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, td, tx, args);
   return cudaGetLastError();
 }
 
 template <int BN, bool A_MN, bool B_MN>
-static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
-                                cudaStream_t s) {
+static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                                const CUtensorMap& tx, const GemmArgs& args, int grid, cudaStream_t s) {
   switch (args.epi) {
-    case EPI_BF16: return launch_one<BN, A_MN, B_MN, EPI_BF16>(ta, tb, args, grid, s);
-    case EPI_F32: return launch_one<BN, A_MN, B_MN, EPI_F32>(ta, tb, args, grid, s);
-    case EPI_F32_ACC: return launch_one<BN, A_MN, B_MN, EPI_F32_ACC>(ta, tb, args, grid, s);
-    case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU>(ta, tb, args, grid, s);
-    case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, args, grid, s);
-    case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, args, grid, s);
-    case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC>(ta, tb, args, grid, s);
+    case EPI_BF16: return launch_one<BN, A_MN, B_MN, EPI_BF16>(ta, tb, td, tx, args, grid, s);
+    case EPI_F32: return launch_one<BN, A_MN, B_MN, EPI_F32>(ta, tb, td, tx, args, grid, s);
+    case EPI_F32_ACC: return launch_one<BN, A_MN, B_MN, EPI_F32_ACC>(ta, tb, td, tx, args, grid, s);
+    case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU>(ta, tb, td, tx, args, grid, s);
+    case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, td, tx, args, grid, s);
+    case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, td, tx, args, grid, s);
+    case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC>(ta, tb, td, tx, args, grid, s);
   }
   return cudaErrorInvalidValue;
 }
 
 template <int BN>
-static cudaError_t dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, bool a_mn,
-                                  bool b_mn, int grid, cudaStream_t s) {
-  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false>(ta, tb, args, grid, s);
-  if (!a_mn && b_mn) return dispatch_epi<BN, false, true>(ta, tb, args, grid, s);
-  if (a_mn && b_mn) return dispatch_epi<BN, true, true>(ta, tb, args, grid, s);
-  return dispatch_epi<BN, true, false>(ta, tb, args, grid, s);
+static cudaError_t dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                                  const CUtensorMap& tx, const GemmArgs& args, bool a_mn, bool b_mn, int grid,
+                                  cudaStream_t s) {
+  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false>(ta, tb, td, tx, args, grid, s);
+  if (!a_mn && b_mn) return dispatch_epi<BN, false, true>(ta, tb, td, tx, args, grid, s);
+  if (a_mn && b_mn) return dispatch_epi<BN, true, true>(ta, tb, td, tx, args, grid, s);
+  return dispatch_epi<BN, true, false>(ta, tb, td, tx, args, grid, s);
 }
 
 int choose_bn(int M, int N, int num_sms) {
@@ -461,10 +545,22 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   if (!p.b_mn) rc = make_tmap_bf16_2d(&tb, p.B, p.N, p.K, p.ldb, 64, bn);
   else rc = make_tmap_bf16_2d(&tb, p.B, p.K, p.N, p.ldb, 64, 64);
   if (rc) return rc - 30;
+  // output (and GELU pre-activation) maps for the TMA-store epilogue
+  CUtensorMap td, tx;
+  const bool out_bf16 = (args.epi == EPI_BF16 || args.epi == EPI_GELU || args.epi == EPI_DGELU);
+  if (out_bf16) rc = make_tmap_2d(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.D, p.M, p.N, args.ldd, 64, 32);
+  else rc = make_tmap_2d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, args.D, p.M, p.N, args.ldd, 32, 32);
+  if (rc) return rc - 40;
+  if (args.epi == EPI_GELU) {
+    rc = make_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.aux, p.M, p.N, args.ld_aux, 64, 32);
+    if (rc) return rc - 50;
+  } else {
+    tx = td;
+  }
   const long units = (long)((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn) * args.splits;
   const int grid = (int)std::min<long>(units, sms);
-  cudaError_t e = (bn == 256) ? dispatch_major<256>(ta, tb, args, p.a_mn, p.b_mn, grid, stream)
-                              : dispatch_major<128>(ta, tb, args, p.a_mn, p.b_mn, grid, stream);
+  cudaError_t e = (bn == 256) ? dispatch_major<256>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream)
+                              : dispatch_major<128>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream);
   return e == cudaSuccess ? 0 : (int)e;
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "gemm_sm100.h"
+#include "symm_mem.h"
 
 namespace mmb {
 
@@ -28,6 +29,7 @@ int embedding_bwd(const long* ids, const float* dout, float* dwte, float* dwpe, 
 
 int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, long n, float lr, float b1, float b2,
                float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s);
+int gelu_fwd_bwd_f32(const float* x, float* y, float* g, long n, int num_sms, cudaStream_t s);
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStream_t s);
 
 int flash_attn_fwd(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, int nh, int d, __nv_bfloat16* out,
@@ -36,5 +38,26 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
                    const __nv_bfloat16* out, const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv,
                    long ld_dqkv, int B, int S, int nh, int d, float softmax_scale, int* err, int num_sms,
                    cudaStream_t stream);
+
+// Fused DP step (fused_dp.cu)
+struct DpPeersHost {
+  int world, rank;
+  void* param[8];
+  void* grad[8];
+  void* pbf16[8];
+  void* sig[8];
+};
+struct DpStepHost {
+  int bucket, epoch;
+  long lo, hi;
+  float* exp_avg;
+  float* exp_avg_sq;
+  float lr, b1, b2, eps, wd, step_size, bc2_sqrt, grad_scale;
+  unsigned* counter;
+  int* err;
+  int max_ctas;
+};
+int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t stream);
+int dp_signal_pad_bytes();
 
 }  // namespace mmb

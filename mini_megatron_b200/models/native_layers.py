@@ -236,11 +236,14 @@ class HeadLossFn(torch.autograd.Function):
             ln_f, lm_head, group, sp, B, vstart, n_valid)
         ctx.x_shape = x.shape
         ctx.mark_non_differentiable(logits)
+        ctx.set_materialize_grads(False)  # no zero-filled [tokens, V] gradient for the logits output
         return loss, logits
 
     @staticmethod
     def backward(ctx, dloss, dlogits_unused):
         x2, m, r, ln_full, logits, lse, lab, wscale = ctx.saved_tensors
+        if dloss is None:
+            dloss = torch.zeros((), device=x2.device)
         scale = (wscale * dloss.float()).contiguous()
         native().ce_bwd(logits, lab, ctx.vstart, ctx.n_valid, lse.contiguous(), scale)   # logits -> dlogits
         w = ctx.lm_head.weight

@@ -1,0 +1,177 @@
+"""ZeRO-1 AdamW fused with the DP gradient reduce-scatter and parameter all-gather.
+
+One kernel per gradient bucket (csrc/fused_dp.cu) runs on a side stream as
+soon as backward has finished every parameter of that bucket:
+
+    peer loads of the owned 1/dp slice of every rank's gradient (NVLink)
+    -> sum, scale by 1/dp -> fp32 AdamW with this rank's sharded moments
+    -> peer stores of the new fp32 parameters and bf16 shadows into every rank
+
+so the data-parallel communication and the whole optimizer step overlap the
+rest of backward, and no rank holds more than 1/dp of the optimizer state.
+The parameter, gradient and bf16 buffers of the model chunk live in one
+symmetric (peer-mapped) allocation together with a signal pad used for the
+cross-rank ready/done flags.  All ranks of the DP group must share a node.
+
+Replaces, for CUDA runs with dp > 1, the reference's per-parameter NCCL
+all-reduce + full AdamW on every rank (parallel/data_parallel.py:5-15,
+main.py:177) and its round-robin ZeRO-1 (parallel/distributed_optimizer.py).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..comm.symmetric import SymmetricBuffer
+from ..ops import native
+from .param_buffer import ParamBuffer
+
+
+class FusedDPOptimizer(torch.optim.Optimizer):
+    def __init__(self, module: torch.nn.Module, dp_group, lr=6e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
+                 bucket_elems=16 << 20, overlap=True, max_ctas=64):
+        C = native()
+        self.group = dp_group
+        self.world = 1 if dp_group is None else dist.get_world_size(dp_group)
+        self.rank = 0 if dp_group is None else dist.get_rank(dp_group)
+        if self.world > 8:
+            raise ValueError("the fused DP kernel supports up to 8 ranks (one NVSwitch node)")
+        self.sig_bytes = (C.dp_signal_pad_bytes() + 4095) // 4096 * 4096
+        self.symm = None
+
+        def allocate(numel):
+            total = self.sig_bytes + numel * (4 + 4 + 2)
+            self.symm = SymmetricBuffer(total, dp_group)
+            self._numel = numel
+            data = self.symm.tensor(self.sig_bytes, numel, torch.float32)
+            grad = self.symm.tensor(self.sig_bytes + 4 * numel, numel, torch.float32)
+            pb = self.symm.tensor(self.sig_bytes + 8 * numel, numel, torch.bfloat16)
+            return data, grad, pb
+
+        self.buf = ParamBuffer(module.parameters(), align=self.world, bucket_elems=bucket_elems, allocator=allocate)
+        if len(self.buf.buckets) > 256:
+            raise ValueError("too many DP buckets for the signal pad; raise bucket size")
+        super().__init__(list(self.buf.params), dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+        n = self._numel
+        self.ptr_param = [self.symm.peer_ptr(r, self.sig_bytes) for r in range(self.world)]
+        self.ptr_grad = [self.symm.peer_ptr(r, self.sig_bytes + 4 * n) for r in range(self.world)]
+        self.ptr_bf16 = [self.symm.peer_ptr(r, self.sig_bytes + 8 * n) for r in range(self.world)]
+        self.ptr_sig = [self.symm.peer_ptr(r, 0) for r in range(self.world)]
+        self.shards = [self.buf.shard_range(b, self.rank) for b in range(len(self.buf.buckets))]
+        self.mom_off = []
+        off = 0
+        for lo, hi in self.shards:
+            self.mom_off.append(off)
+            off += hi - lo
+        dev = self.buf.data.device
+        self.exp_avg = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(off, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(len(self.buf.buckets), dtype=torch.int32, device=dev)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.overlap = overlap
+        self._default_overlap = overlap
+        self.max_ctas = max_ctas
+        self._step = 0
+        self._epoch = 0
+        self._bucket_of = {}
+        for b, (_, _, params) in enumerate(self.buf.buckets):
+            for p in params:
+                self._bucket_of[id(p)] = b
+        self._pending = []
+        self._next = 0
+        # every rank's buffers hold the same initial values (same seed) -- make the bf16 shadow current
+        self.buf.refresh_bf16()
+        if self.world > 1:
+            dist.barrier(group=dp_group)
+
+    # ----------------------------------------------------------- GradSync interface
+    @property
+    def active(self):
+        return True
+
+    def reset(self):
+        """Start a new optimizer step: new epoch for the cross-rank flags."""
+        self._pending = [len(params) for (_, _, params) in self.buf.buckets]
+        self._next = 0
+        self._launched_step = False
+
+    def attach(self, modules):
+        for m in modules:
+            params = [p for p in m.parameters() if id(p) in self._bucket_of]
+            hooks = list(getattr(m, "_mmb_grad_ready_hooks", ()))
+            hooks.append(lambda ps=params: self.mark_ready(ps))
+            m._mmb_grad_ready_hooks = hooks
+
+    def mark_ready(self, params):
+        if not self.overlap:
+            return
+        for p in params:
+            b = self._bucket_of.get(id(p))
+            if b is not None:
+                self._pending[b] -= 1
+        while self._next < len(self._pending) and self._pending[self._next] <= 0:
+            self._launch(self._next)
+            self._next += 1
+
+    def _begin(self):
+        if not self._launched_step:
+            self._launched_step = True
+            self._step += 1
+            self._epoch += 1
+
+    def _launch(self, b):
+        self._begin()
+        C = native()
+        g = self.param_groups[0]
+        lo, hi = self.shards[b]
+        n = hi - lo
+        off = self.mom_off[b]
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream())
+        self.stream.wait_event(ev)
+        with torch.cuda.stream(self.stream):
+            C.dp_rs_adamw_ag(self.ptr_param, self.ptr_grad, self.ptr_bf16, self.ptr_sig, self.rank, b, self._epoch,
+                             lo, hi, self.exp_avg[off:off + n], self.exp_avg_sq[off:off + n], self.counters[b:b + 1],
+                             g["lr"], g["betas"][0], g["betas"][1], g["eps"], g["weight_decay"], self._step,
+                             1.0 / self.world, self.max_ctas)
+
+    def finish(self):
+        """Launch the buckets not yet issued (in order)."""
+        while self._next < len(self.buf.buckets):
+            self._launch(self._next)
+            self._next += 1
+
+    # ----------------------------------------------------------- optimizer interface
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        self.finish()
+        torch.cuda.current_stream().wait_stream(self.stream)
+        self.overlap = self._default_overlap
+        return loss
+
+    def zero_grad(self, set_to_none: bool = False):
+        self.buf.zero_grad()
+
+    def state_dict(self):
+        return {"step": self._step, "epoch": self._epoch, "dp_rank": self.rank, "dp_size": self.world,
+                "shards": list(self.shards), "exp_avg": self.exp_avg.clone(), "exp_avg_sq": self.exp_avg_sq.clone(),
+                "param_groups": [{k: v for k, v in g.items() if k != "params"} for g in self.param_groups]}
+
+    def load_state_dict(self, sd):
+        if sd["dp_size"] != self.world or list(map(tuple, sd["shards"])) != list(map(tuple, self.shards)):
+            raise ValueError("fused-DP state was saved with a different DP layout")
+        self._step = int(sd["step"])
+        self.exp_avg.copy_(sd["exp_avg"])
+        self.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        for g, s in zip(self.param_groups, sd["param_groups"]):
+            g.update(s)
+        self.buf.refresh_bf16()
+
+    def close(self):
+        if self.symm is not None:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self.symm.close()
+            self.symm = None

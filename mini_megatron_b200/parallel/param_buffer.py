@@ -43,7 +43,7 @@ class ParamBuffer:
     """
 
     def __init__(self, params: Iterable[torch.nn.Parameter], device=None, align: int = 1,
-                 bf16_shadow: bool = True, bucket_elems: int = 0):
+                 bf16_shadow: bool = True, bucket_elems: int = 0, allocator=None):
         params = [p for p in params if p.requires_grad]
         # de-duplicate shared parameters
         seen, uniq = set(), []
@@ -70,9 +70,13 @@ class ParamBuffer:
         self.numel = max(off, bucket_quant)
         if not self.buckets:
             self.buckets.append((0, self.numel, []))
-        self.data = torch.zeros(self.numel, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
-        self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=device) if bf16_shadow else None
+        if allocator is not None:
+            # caller-provided storage (e.g. one symmetric allocation shared with NVLink peers)
+            self.data, self.grad, self.bf16 = allocator(self.numel)
+        else:
+            self.data = torch.zeros(self.numel, dtype=torch.float32, device=device)
+            self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
+            self.bf16 = torch.zeros(self.numel, dtype=torch.bfloat16, device=device) if bf16_shadow else None
         for p, o in zip(self.params, self.offsets):
             n = p.numel()
             view = self.data[o:o + n].view_as(p)

@@ -75,6 +75,7 @@ class TrainConfig:
     warmup_steps: int = 10
     num_steps: int = 100
     dp_overlap: bool = True
+    dp_impl: str = "auto"               # "fused" (NVLink kernel), "nccl", or "auto" (fused on CUDA when dp > 1)
     bucket_mb: float = 64.0
     recompute: bool = False
     average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
@@ -109,14 +110,26 @@ class Trainer:
         self.model.to(self.device)
         dp = mpu["dp_size"]
         bucket_elems = int(cfg.bucket_mb * (1 << 20) / 4)
-        self.buf = make_param_buffer(self.model, align=dp, bucket_elems=bucket_elems)
         grad_scale = 1.0 / dp
-        if cfg.zero1:
+        impl = cfg.dp_impl
+        if impl == "auto":
+            impl = "fused" if (self.device.type == "cuda" and dp > 1 and not sp) else "nccl"
+        self.dp_impl = impl
+        if impl == "fused":
+            from .parallel.fused_dp import FusedDPOptimizer
+            self.optimizer = FusedDPOptimizer(self.model, mpu["dp_group"], lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                              weight_decay=cfg.weight_decay, bucket_elems=bucket_elems,
+                                              overlap=cfg.dp_overlap)
+            self.buf = self.optimizer.buf
+            self.grad_sync = self.optimizer
+        elif cfg.zero1:
+            self.buf = make_param_buffer(self.model, align=dp, bucket_elems=bucket_elems)
             self.optimizer = DistributedOptimizer(self.buf, mpu["dp_group"], lr=cfg.lr, betas=cfg.betas,
                                                   eps=cfg.eps, weight_decay=cfg.weight_decay,
                                                   overlap=cfg.dp_overlap)
             self.grad_sync = self.optimizer.grad_sync
         else:
+            self.buf = make_param_buffer(self.model, align=dp, bucket_elems=bucket_elems)
             self.optimizer = FusedAdamW(self.model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                         weight_decay=cfg.weight_decay, grad_scale=grad_scale)
             self.grad_sync = GradSync(self.buf, mpu["dp_group"], mode="allreduce", overlap=cfg.dp_overlap)
@@ -176,7 +189,7 @@ class Trainer:
             losses = self.engine.run(batch_fn, m, loss_scale=scale, pre_backward=pre_backward)
             result = torch.stack([l.detach() for l in losses]).mean() if losses else None
         self.grad_sync.overlap = cfg.dp_overlap
-        if not cfg.zero1:
+        if not cfg.zero1 and self.dp_impl != "fused":
             self.grad_sync.finish()
         if self.sp_params:
             allreduce_sequence_parallel_grads(self.sp_params, self.mpu["tp_group"])
@@ -190,6 +203,8 @@ class Trainer:
         return self.model, self.optimizer, self.scheduler
 
     def destroy(self):
+        if hasattr(self.optimizer, "close"):
+            self.optimizer.close()
         pg.set_model_parallel(None)
 
 

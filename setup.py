@@ -12,7 +12,8 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("mini_megatron_b200", "csrc")
 
-sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
+sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp"),
+                                                           os.path.join(CSRC, "symm_mem.cpp")]
 
 NVCC_FLAGS = [
     "-O3",

@@ -114,3 +114,14 @@ def test_adamw_matches_torch():
     torch.cuda.synchronize()
     torch.testing.assert_close(p, ref.detach(), rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(pb.float(), p.bfloat16().float())
+
+
+def test_gelu_math_matches_exact_erf_gelu():
+    C = _C()
+    x = torch.linspace(-12, 12, 1_000_001, device="cuda")
+    y, g = C.gelu_fwd_bwd_f32(x)
+    xr = x.double().requires_grad_(True)
+    yr = torch.nn.functional.gelu(xr)
+    yr.backward(torch.ones_like(yr))
+    assert (y.double() - yr).abs().max().item() < 2e-6
+    assert (g.double() - xr.grad).abs().max().item() < 2e-6

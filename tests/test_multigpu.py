@@ -1,0 +1,105 @@
+"""Multi-GPU checks (need >= 2 GPUs; skipped otherwise).
+
+* fused DP (NVLink reduce-scatter + AdamW + all-gather kernel) gives the same
+  parameters as the NCCL all-reduce path after several steps;
+* native TP=2 (with and without sequence parallelism) and PP=2 reproduce the
+  single-GPU loss of the same model.
+"""
+import os
+import tempfile
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+NEED2 = pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+
+CFG = dict(num_layers=2, hidden_size=256, num_attention_heads=4, ffn_hidden_size=1024, max_seq_len=256,
+           vocab_size=1000)
+
+
+def _entry(rank, world, port, fn, args, out):
+    import datetime
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        res = fn(rank, world, *args)
+        torch.save(res, os.path.join(out, f"r{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(fn, world, *args, port=29711):
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.get_context("spawn")
+        ps = [ctx.Process(target=_entry, args=(r, world, port, fn, args, d)) for r in range(world)]
+        for p in ps:
+            p.start()
+        for p in ps:
+            p.join(300)
+            if p.is_alive():
+                p.kill()
+        assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+        return [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
+
+
+def _train(rank, world, tp, pp, sp, dp_impl, steps, micro):
+    from mini_megatron_b200.config import GPTConfig
+    from mini_megatron_b200.training import TrainConfig, Trainer, synthetic_batch
+    cfg = TrainConfig(model=GPTConfig(**CFG), micro_batch_size=2, seq_len=256, num_microbatches=micro, tp=tp, pp=pp,
+                      sequence_parallel=sp, dp_impl=dp_impl, lr=1e-3, warmup_steps=0, num_steps=100,
+                      bucket_mb=1.0)
+    t = Trainer(cfg)
+    dp_rank = t.mpu["dp_rank"]
+    losses = []
+    for s in range(steps):
+        tok, lab = synthetic_batch(micro, 2, 256, CFG["vocab_size"], seed=100 * s + dp_rank)
+        loss = t.train_step(tok, lab)
+        losses.append(None if loss is None else loss.item())
+    torch.cuda.synchronize()
+    from mini_megatron_b200.ops import check_errors
+    check_errors()
+    state = {k: v.detach().float().cpu() for k, v in t.model.state_dict().items()}
+    t.destroy()
+    return {"losses": losses, "state": state}
+
+
+@NEED2
+def test_fused_dp_matches_nccl_dp():
+    fused = _run(_train, 2, 1, 1, False, "fused", 3, 1, port=29711)
+    nccl = _run(_train, 2, 1, 1, False, "nccl", 3, 1, port=29712)
+    for r in range(2):
+        for k, v in fused[r]["state"].items():
+            ref = nccl[r]["state"][k]
+            rel = ((v - ref).norm() / (ref.norm() + 1e-12)).item()
+            assert rel < 1e-4, (k, rel)
+    # replicas agree with each other exactly (both received the same all-gathered parameters)
+    for k in fused[0]["state"]:
+        assert torch.equal(fused[0]["state"][k], fused[1]["state"][k]), k
+
+
+@NEED2
+@pytest.mark.parametrize("sp", [False, True])
+def test_native_tp2_first_step_loss_matches_tp1(sp):
+    ref = _run(_train, 1, 1, 1, False, "nccl", 1, 1, port=29713)[0]["losses"][0]
+    res = _run(_train, 2, 2, 1, sp, "nccl", 2, 1, port=29714 + int(sp))
+    # TP shards are initialised independently (as in the reference), so only the first-step loss
+    # (~ln V for a random model) is comparable; training must also proceed without error
+    for r in res:
+        assert abs(r["losses"][0] - ref) < 0.05, (r["losses"], ref)
+
+
+@NEED2
+def test_native_pp2_runs_and_loss_is_sane():
+    res = _run(_train, 2, 1, 2, False, "nccl", 3, 4, port=29716)
+    last = res[1]["losses"]
+    assert all(x is not None for x in last) and abs(last[0] - 6.9) < 0.3, last
+    assert res[0]["losses"] == [None, None, None]
