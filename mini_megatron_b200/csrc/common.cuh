@@ -1,8 +1,8 @@
 // Shared device helpers for the sm_100a kernels of this package.
 //
 // Everything here is thin inline PTX around the Blackwell primitives the kernels
-// are built from: mbarriers (with bounded waits), TMA tile loads (never with
-// cluster multicast), tcgen05 MMA / TMEM allocation / TMEM loads, and the
+// are built from: mbarriers (with bounded waits), TMA tile loads (each into the
+// issuing CTA's own shared memory only), tcgen05 MMA / TMEM allocation / TMEM loads, and the
 // shared-memory matrix descriptor used by tcgen05.mma.
 #pragma once
 
@@ -90,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // ---------------------------------------------------------------- TMA
 // 2-D tiled bulk tensor load global -> shared, completion signalled on an
-// mbarrier (transaction bytes).  Plain (non-multicast) form only.
+// mbarrier (transaction bytes).  Single-destination form only.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {
   asm volatile(
