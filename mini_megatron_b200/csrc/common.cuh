@@ -279,7 +279,8 @@ struct GeluTerms {
 };
 __device__ __forceinline__ GeluTerms gelu_terms(float x) {
   const float z = fabsf(x) * 0.70710678118654752f;
-  const float t = __frcp_rn(1.0f + 0.3275911f * z);
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(1.0f + 0.3275911f * z));
   const float e = __expf(-z * z);
   const float poly = t * (0.254829592f + t * (-0.284496736f + t * (1.421413741f + t * (-1.453152027f + t * 1.061405429f))));
   const float erf_abs = 1.0f - poly * e;

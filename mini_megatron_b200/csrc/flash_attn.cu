@@ -41,15 +41,17 @@ template <int D>
 struct FwdCfg {
   static constexpr int CHUNKS = D / 64;                 // 64-column (128 B) chunks per row
   static constexpr int TILE_BYTES = BM * D * 2;         // one Q / K / V tile
-  static constexpr int P_BUFS = (D == 64) ? 2 : 1;
+  static constexpr int P_BUFS = 1;
+  static constexpr int V_STAGES = (D == 64) ? 1 : 2;    // d=64: two CTAs per SM, so keep smem <= ~100 KB
   static constexpr int P_BYTES = BM * BN * 2;           // 32 KB
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + TILE_BYTES;
   static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
-  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;
+  static constexpr int P_OFF = V_OFF + V_STAGES * TILE_BYTES;
   static constexpr int BAR_OFF = P_OFF + P_BUFS * P_BYTES;
   static constexpr int SMEM = 1024 + BAR_OFF + 256;
   static constexpr int TMEM_COLS = (BN + 2 * D) <= 256 ? 256 : 512;
+  static constexpr int MIN_CTAS = (D == 64) ? 2 : 1;
 };
 
 struct FwdArgs {
@@ -77,7 +79,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const FwdArgs a) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -89,9 +91,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sP = smem + C::P_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2]
-  uint64_t* v_full = bars + 3;    // [2]
-  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* k_full = bars + 1;    // [2]  K stage loaded
+  uint64_t* v_full = bars + 3;    // [2]  V stage loaded
+  uint64_t* k_empty = bars + 5;   // [2]  S MMA that read the K stage is done
   uint64_t* s_full = bars + 7;
   uint64_t* s_free = bars + 8;
   uint64_t* p_full = bars + 9;    // [2]
@@ -99,7 +101,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* o_full = bars + 13;   // [2]
   uint64_t* o_free = bars + 15;   // [2]
   uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* v_empty = bars + 18;  // [2]  PV MMA that read the V stage is done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -115,7 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&p_free[i], 1);
       mbar_init(&o_full[i], 1);
@@ -147,15 +151,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(sQ + c * 16384, &tm_qkv, q_full, qx + 64 * c, row0 + qt * BM);
       for (int j = 0; j < J; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, a.err, kErrAttnWait, abort_flag)) break;
+        const int vs = j % C::V_STAGES;
+        if (j >= 2 && !mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1, a.err, kErrAttnWait, abort_flag)) break;
         uint8_t* kd = sK + st * C::TILE_BYTES;
-        uint8_t* vd = sV + st * C::TILE_BYTES;
         mbar_expect_tx(&k_full[st], C::TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(kd + c * 16384, &tm_qkv, &k_full[st], kx + 64 * c, row0 + j * BN);
-        mbar_expect_tx(&v_full[st], C::TILE_BYTES);
+        if (j >= C::V_STAGES &&
+            !mbar_wait(&v_empty[vs], ((j / C::V_STAGES) - 1) & 1, a.err, kErrAttnWait, abort_flag))
+          break;
+        uint8_t* vd = sV + vs * C::TILE_BYTES;
+        mbar_expect_tx(&v_full[vs], C::TILE_BYTES);
 #pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(vd + c * 16384, &tm_qkv, &v_full[st], vx + 64 * c, row0 + j * BN);
+        for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(vd + c * 16384, &tm_qkv, &v_full[vs], vx + 64 * c, row0 + j * BN);
       }
     }
   } else if (warp == 1) {
@@ -165,13 +173,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(q_full, 0, a.err, kErrAttnWait, abort_flag);
       const uint32_t q_addr = smem_u32(sQ);
       auto issue_pv = [&](int t) -> bool {
-        const int st = t & 1, pb = t % C::P_BUFS, ob = t & 1;
-        if (!mbar_wait(&v_full[st], (t >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
+        const int vs = t % C::V_STAGES, pb = t % C::P_BUFS, ob = t & 1;
+        if (!mbar_wait(&v_full[vs], (t / C::V_STAGES) & 1, a.err, kErrAttnWait, abort_flag)) return false;
         if (!mbar_wait(&p_full[pb], (t / C::P_BUFS) & 1, a.err, kErrAttnWait, abort_flag)) return false;
         if (t >= 2 && !mbar_wait(&o_free[ob], ((t - 2) >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
         tc_fence_after();
         const uint32_t p_addr = smem_u32(sP + pb * C::P_BYTES);
-        const uint32_t v_addr = smem_u32(sV + st * C::TILE_BYTES);
+        const uint32_t v_addr = smem_u32(sV + vs * C::TILE_BYTES);
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
           const uint64_t ad = make_sdesc_sw128(p_addr + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024);
@@ -180,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(&o_full[ob]);
         umma_commit(&p_free[pb]);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[vs]);
         return true;
       };
       for (int j = 0; j < J && ok; ++j) {
@@ -196,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_bf16_ss(t_s, ad, bd, idesc_s, k != 0 ? 1u : 0u);
         }
         umma_commit(s_full);
+        umma_commit(&k_empty[st]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_pv(J - 1);

@@ -311,46 +311,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
                            pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
         } else if constexpr (EPI == EPI_GELU) {
-          // stage <- pre-activation, store it (aux); then stage <- gelu, stored below (D)
+          // gelu and gelu' share one erf evaluation; gelu' is stored (aux) for the backward
+          uint32_t act[W / 2], grd[W / 2];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float* x = v + 8 * u;
-            *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
-                make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
-                           pack_bf16x2(x[6], x[7]));
+          for (int i = 0; i < W; i += 2) {
+            const GeluTerms g0 = gelu_terms(v[i]), g1 = gelu_terms(v[i + 1]);
+            act[i >> 1] = pack_bf16x2(v[i] * g0.cdf, v[i + 1] * g1.cdf);
+            grd[i >> 1] = pack_bf16x2(g0.cdf + v[i] * g0.pdf, g1.cdf + v[i + 1] * g1.pdf);
           }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
+                make_uint4(grd[4 * u], grd[4 * u + 1], grd[4 * u + 2], grd[4 * u + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
             tma_store_2d(&tmAux, stg, col0, r0);
             bulk_commit();
+            bulk_wait_read<0>();
           }
-#pragma unroll
-          for (int i = 0; i < W; ++i) v[i] = gelu_f(v[i]);
-          if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float* x = v + 8 * u;
+          for (int u = 0; u < 8; ++u)
             *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
-                make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
-                           pack_bf16x2(x[6], x[7]));
-          }
+                make_uint4(act[4 * u], act[4 * u + 1], act[4 * u + 2], act[4 * u + 3]);
         } else if constexpr (EPI == EPI_DGELU) {
-          // stage <- pre-activation tile (coalesced), then out = acc * gelu'(pre) in place
+          // stage <- gelu'(pre) tile (coalesced), then out = acc * gelu' in place
           const uint8_t* src = reinterpret_cast<const uint8_t*>(args.aux) + ((size_t)r0 * args.ld_aux + col0) * 2;
           stage_load(stg, src, args.ld_aux * 2, rows_valid, colb_valid, lane);
           __syncwarp();
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             uint4* pu = reinterpret_cast<uint4*>(stage_unit(stg, lane, u));
-            uint4 pre = *pu;
-            const uint32_t* pw = reinterpret_cast<const uint32_t*>(&pre);
+            uint4 gp = *pu;
+            const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gp);
             uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float2 pf = unpack_bf16x2(pw[e]);
-              o[e] = pack_bf16x2(v[8 * u + 2 * e] * gelu_grad_f(pf.x), v[8 * u + 2 * e + 1] * gelu_grad_f(pf.y));
+              const float2 gf = unpack_bf16x2(gw[e]);
+              o[e] = pack_bf16x2(v[8 * u + 2 * e] * gf.x, v[8 * u + 2 * e + 1] * gf.y);
             }
             *pu = make_uint4(o[0], o[1], o[2], o[3]);
           }

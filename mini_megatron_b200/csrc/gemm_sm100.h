@@ -10,9 +10,9 @@ enum GemmEpilogue : int {
   EPI_BF16 = 0,     // D(bf16)  = alpha*acc
   EPI_F32 = 1,      // D(fp32)  = alpha*acc
   EPI_F32_ACC = 2,  // D(fp32) += alpha*acc            (gradient accumulation)
-  EPI_GELU = 3,     // aux(bf16) = alpha*acc ; D(bf16) = gelu(alpha*acc)
+  EPI_GELU = 3,     // x = alpha*acc: D(bf16) = gelu(x), aux(bf16) = gelu'(x)  (saved for the backward)
   EPI_RESID = 4,    // D(fp32)  = resid(fp32) + alpha*acc (resid may alias D)
-  EPI_DGELU = 5,    // D(bf16)  = alpha*acc * gelu'(aux(bf16))
+  EPI_DGELU = 5,    // D(bf16)  = alpha*acc * aux(bf16)          (aux = gelu'(pre) from EPI_GELU)
   EPI_F32_ATOMIC = 6,  // D(fp32) += alpha*acc with atomics (split-K partial sums)
 };
 

@@ -89,25 +89,25 @@ def _layer_forward(x2, layer, B, S, group, sp):
         x1 = x2 + _reduce(part, B, group, sp).float()
     ln2, m2, r2 = _ln_fwd(x1, layer.ln2)
     ln2_full = _gather_seq(ln2, B, group) if sp else ln2
-    act, pre = linear_gelu_fwd(ln2_full, bf16_weight(mlp.fc1.weight))
+    act, gelu_grad = linear_gelu_fwd(ln2_full, bf16_weight(mlp.fc1.weight))
     if t == 1:
         out = linear_fwd(act, bf16_weight(mlp.fc2.weight), out=torch.empty_like(x1), epi=EPI_RESID, resid=x1)
     else:
         part = linear_fwd(act, bf16_weight(mlp.fc2.weight))
         out = x1 + _reduce(part, B, group, sp).float()
-    saved = (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, pre, act)
+    saved = (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, gelu_grad, act)
     return out, saved
 
 
 def _layer_backward(dout, saved, layer, B, S, group, sp):
     attn, mlp = layer.attn, layer.mlp
     t = _world(group)
-    (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, pre, act) = saved
+    (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, gelu_grad, act) = saved
     # ---- MLP
     g = dout.to(torch.bfloat16)
     g_full = _gather_seq(g, B, group) if sp else g
     w2, w1 = mlp.fc2.weight, mlp.fc1.weight
-    d_pre = linear_dgrad(g_full, bf16_weight(w2), epi=EPI_DGELU, aux=pre)
+    d_pre = linear_dgrad(g_full, bf16_weight(w2), epi=EPI_DGELU, aux=gelu_grad)
     linear_wgrad(g_full, act, grad_target(w2))
     d_ln2 = linear_dgrad(d_pre, bf16_weight(w1))
     linear_wgrad(d_pre, ln2_full, grad_target(w1))

@@ -32,11 +32,14 @@ def linear_fwd(x2d, w, out=None, epi=EPI_BF16, aux=None, resid=None, alpha=1.0):
 
 
 def linear_gelu_fwd(x2d, w):
-    """(gelu(x W^T), x W^T) both bf16 -- fc1 with the GELU fused in the epilogue."""
-    pre = torch.empty(x2d.shape[0], w.shape[0], device=x2d.device, dtype=torch.bfloat16)
-    act = torch.empty_like(pre)
-    native().gemm(x2d, False, w, False, act, EPI_GELU, aux=pre)
-    return act, pre
+    """(gelu(h), gelu'(h)) with h = x W^T, both bf16 -- fc1 with the GELU fused in the epilogue.
+
+    The derivative is saved instead of h: the backward's fc2 dgrad epilogue then
+    only multiplies by it (EPI_DGELU)."""
+    grad = torch.empty(x2d.shape[0], w.shape[0], device=x2d.device, dtype=torch.bfloat16)
+    act = torch.empty_like(grad)
+    native().gemm(x2d, False, w, False, act, EPI_GELU, aux=grad)
+    return act, grad
 
 
 def linear_dgrad(dy2d, w, out=None, epi=EPI_BF16, aux=None):

@@ -74,18 +74,19 @@ def test_gemm_gelu_and_dgelu():
     M, N, K = 512, 1024, 256
     A, B, ref = _operands(M, N, K, False, False, seed=3)
     D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    pre = torch.empty_like(D)
-    C.gemm(A, False, B, False, D, C.EPI_GELU, aux=pre)
+    gp = torch.empty_like(D)
+    C.gemm(A, False, B, False, D, C.EPI_GELU, aux=gp)
     torch.cuda.synchronize()
-    _check_close(pre, ref, 1e-2)
-    _check_close(D, torch.nn.functional.gelu(ref), 1e-2)
-    # dgelu: out = acc * gelu'(pre)
+    x = ref.clone().requires_grad_(True)
+    y = torch.nn.functional.gelu(x)
+    y.backward(torch.ones_like(y))
+    _check_close(D, y.detach(), 1e-2)
+    _check_close(gp, x.grad, 1e-2)
+    # dgelu: out = acc * gelu'(pre), with gelu'(pre) as stored by the forward epilogue
     D2 = torch.empty_like(D)
-    C.gemm(A, False, B, False, D2, C.EPI_DGELU, aux=pre)
+    C.gemm(A, False, B, False, D2, C.EPI_DGELU, aux=gp)
     torch.cuda.synchronize()
-    x = pre.float().requires_grad_(True)
-    torch.nn.functional.gelu(x).backward(torch.ones_like(x))
-    _check_close(D2, ref * x.grad, 2e-2)
+    _check_close(D2, ref * gp.float(), 1e-2)
 
 
 def test_gemm_residual_inplace():
