@@ -66,13 +66,71 @@ def bench_gemm(args):
     assert _C.get_error() == 0
 
 
+def profile_case(args):
+    """One launch of each hot kernel on GPT-125M training shapes (B=16, S=1024): the ncu target.
+
+    Order of launches (use ncu -k to pick one): GEMM fc1 fwd (GELU epilogue),
+    GEMM o fwd (residual epilogue), GEMM fc2 dgrad (GELU-backward epilogue),
+    GEMM fc1 wgrad (split-K reduce-add), attention fwd, attention bwd, LayerNorm
+    fwd/bwd, cross-entropy fwd/bwd, AdamW over 162M parameters.  Everything is
+    allocated up front (about 4 GB).
+    """
+    from mini_megatron_b200 import _C
+    torch.manual_seed(0)
+    T, H, F, V, nh, S = args.tokens, 768, 3072, 50304, 12, 1024
+    B = T // S
+    bf = dict(device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(T, H, **bf)
+    w1 = torch.randn(F, H, **bf) * 0.02
+    w2 = torch.randn(H, F, **bf) * 0.02
+    wo = torch.randn(H, H, **bf) * 0.02
+    act = torch.empty(T, F, **bf)
+    gp = torch.empty(T, F, **bf)
+    resid = torch.randn(T, H, device="cuda")
+    out32 = torch.empty(T, H, device="cuda")
+    dy = torch.randn(T, H, **bf)
+    dpre = torch.empty(T, F, **bf)
+    dw1 = torch.zeros(F, H, device="cuda")
+    qkv = torch.randn(T, 3 * H, **bf)
+    lnx = torch.randn(T, H, device="cuda")
+    g = torch.ones(H, device="cuda")
+    bvec = torch.zeros(H, device="cuda")
+    lny = torch.empty(T, H, **bf)
+    mean = torch.empty(T, device="cuda")
+    rstd = torch.empty(T, device="cuda")
+    dx = torch.empty(T, H, device="cuda")
+    logits = torch.randn(T, V, **bf)
+    labels = torch.randint(0, 50257, (T,), device="cuda")
+    n_par = 162_000_000
+    p = torch.randn(n_par, device="cuda")
+    gr = torch.randn(n_par, device="cuda")
+    m = torch.zeros(n_par, device="cuda")
+    v = torch.zeros(n_par, device="cuda")
+    pb = torch.empty(n_par, **bf)
+    for _ in range(2):  # warm-up pass, then the profiled pass
+        _C.gemm(x, False, w1, False, act, _C.EPI_GELU, aux=gp)
+        _C.gemm(x, False, wo, False, out32, _C.EPI_RESID, resid=resid)
+        _C.gemm(dy, False, w2, True, dpre, _C.EPI_DGELU, aux=gp)
+        _C.gemm(dpre, True, x, True, dw1, _C.EPI_F32_ACC)
+        o, lse = _C.flash_attn_fwd(qkv, B, S, nh, 64)
+        _C.flash_attn_bwd(dy, qkv, o, lse, B, S, nh, 64)
+        _C.layernorm_fwd(lnx, g, bvec, lny, mean, rstd, 1e-5)
+        _C.layernorm_bwd(dy, lnx, mean, rstd, g, resid, dx, g.clone(), bvec.clone())
+        mx, se, tg = _C.ce_fwd_stats(logits, labels, 0, 50257)
+        _C.ce_bwd(logits, labels, 0, 50257, (mx + torch.log(se)).contiguous(), torch.full((T,), 1.0 / T, device="cuda"))
+        _C.adamw_flat(p, gr, m, v, pb, 1e-3, 0.9, 0.999, 1e-8, 0.1, 1, 1.0)
+        torch.cuda.synchronize()
+    assert _C.get_error() == 0
+    print("profile case done")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm"])
+    ap.add_argument("kernel", choices=["gemm", "profile"])
     ap.add_argument("--model", default="gpt-125m")
     ap.add_argument("--tokens", type=int, default=16384)
     args = ap.parse_args()
-    {"gemm": bench_gemm}[args.kernel](args)
+    {"gemm": bench_gemm, "profile": profile_case}[args.kernel](args)
 
 
 if __name__ == "__main__":
