@@ -135,7 +135,8 @@ void layernorm_fwd(const Tensor& x, const Tensor& gamma, const Tensor& beta, Ten
 
 // dx = LN_bwd(dy) (+ dres); dgamma/dbeta accumulated (+=) into the given fp32 buffers.
 void layernorm_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd, const Tensor& gamma,
-                   const c10::optional<Tensor>& dres, Tensor& dx, Tensor& dgamma, Tensor& dbeta) {
+                   const c10::optional<Tensor>& dres, Tensor& dx, Tensor& dgamma, Tensor& dbeta,
+                   const c10::optional<Tensor>& dx_bf16) {
   check_bf16(dy, "dy");
   check_f32(x, "x");
   check_f32(dx, "dx");
@@ -148,10 +149,16 @@ void layernorm_bwd(const Tensor& dy, const Tensor& x, const Tensor& mean, const 
     check_f32(*dres, "dres");
     dr = dres->data_ptr<float>();
   }
-  const int rc = mmb::layernorm_bwd(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), x.data_ptr<float>(),
-                                    mean.data_ptr<float>(), rstd.data_ptr<float>(), gamma.data_ptr<float>(), dr,
-                                    dx.data_ptr<float>(), part.data_ptr<float>(), dgamma.data_ptr<float>(),
-                                    dbeta.data_ptr<float>(), rows, H, nparts, cur_stream());
+  __nv_bfloat16* xb = nullptr;
+  if (dx_bf16.has_value()) {
+    check_bf16(*dx_bf16, "dx_bf16");
+    TORCH_CHECK(dx_bf16->numel() == dx.numel(), "dx_bf16 size mismatch");
+    xb = reinterpret_cast<__nv_bfloat16*>(dx_bf16->data_ptr());
+  }
+  const int rc = mmb::layernorm_bwd2(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), x.data_ptr<float>(),
+                                     mean.data_ptr<float>(), rstd.data_ptr<float>(), gamma.data_ptr<float>(), dr,
+                                     dx.data_ptr<float>(), xb, part.data_ptr<float>(), dgamma.data_ptr<float>(),
+                                     dbeta.data_ptr<float>(), rows, H, nparts, cur_stream());
   MMB_CHECK_RC(rc, "layernorm_bwd");
 }
 
@@ -374,7 +381,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b_mn"), py::arg("D"), py::arg("epi"), py::arg("aux") = c10::nullopt,
         py::arg("resid") = c10::nullopt, py::arg("alpha") = 1.0, py::arg("bn") = 0);
   m.def("layernorm_fwd", &layernorm_fwd);
-  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
+        py::arg("gamma"), py::arg("dres"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"),
+        py::arg("dx_bf16") = c10::nullopt);
   m.def("ce_fwd_stats", &ce_fwd_stats);
   m.def("ce_bwd", &ce_bwd);
   m.def("embedding_fwd", &embedding_fwd);

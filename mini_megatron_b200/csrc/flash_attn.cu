@@ -399,12 +399,15 @@ struct BwdCfg {
   static constexpr int PT_OFF = DO_OFF + STAGES * TILE;
   static constexpr int DS_OFF = PT_OFF + BM * BN * 2;
   static constexpr int LD_OFF = DS_OFF + BM * BN * 2;   // per stage: lse[128], delta[128]
-  static constexpr int BAR_OFF = LD_OFF + STAGES * 1024;
+  static constexpr int DQ_OFF = LD_OFF + STAGES * 1024;  // 8 warps x 4 KB dQ staging for the bulk reduce-add
+  static constexpr int BAR_OFF = DQ_OFF + 8 * 4096;
   static constexpr int SMEM = 1024 + BAR_OFF + 256;
   // TMEM columns
   static constexpr int T_ST = 0, T_DPT = 128, T_DV = 256, T_DK = 256 + D;
   static constexpr int T_DQ = (D == 64) ? 384 : 128;   // D=128: dQ reuses the dP^T columns
 };
+
+constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, 8 softmax-gradient warps
 
 struct BwdArgs {
   int B, S, nh;
@@ -429,9 +432,9 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                     const BwdArgs a) {
+                     const __grid_constant__ CUtensorMap tm_dq, const BwdArgs a) {
   using C = BwdCfg<D>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -444,6 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sPT = smem + C::PT_OFF;
   uint8_t* sDS = smem + C::DS_OFF;
   float* sLD = reinterpret_cast<float*>(smem + C::LD_OFF);
+  uint8_t* sDQ = smem + C::DQ_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* kv_full = bars + 0;
   uint64_t* q_full = bars + 1;    // [2]
@@ -475,17 +479,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_empty[i], 1);
     }
     mbar_init(st_full, 1);
-    mbar_init(st_free, 128);
-    mbar_init(ps_full, 128);
+    mbar_init(st_free, 256);
+    mbar_init(ps_full, 256);
     mbar_init(ps_free, 1);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 256);
     mbar_init(dkv_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_qkv);
     prefetch_tmap(&tm_do);
+    prefetch_tmap(&tm_dq);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -588,27 +593,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    // warps 2..9: w and w+4 share a TMEM lane quarter; `half` selects which 64 query columns
+    // of S^T / dP^T (and which half of the dQ / dK / dV columns) this warp handles.
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int c = q * 32 + lane;               // key row (TMEM lane) for S^T / dP^T / dK / dV
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const float sl2 = a.scale_log2;
+    uint8_t* stg = sDQ + (warp - 2) * 4096;
     bool ok = true;
 
+    // dQ_t (TMEM lane = query row) -> per-warp 32x32 fp32 stage -> one bulk tensor reduce-add into dq_acc
     auto drain_dq = [&](int t) -> bool {
       if (!warp_wait(dq_full, t & 1, a.err, kErrAttnWait, abort_flag)) return false;
       tc_fence_after();
-      const int qrow = row0 + (j + t) * BM + c;  // TMEM lane = query row for dQ
-      float* dst = a.dq_acc + (size_t)qrow * a.ld_dq + h * D;
+      const int qrow0 = row0 + (j + t) * BM + q * 32;
 #pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = half; cc < D / 32; cc += 2) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem + C::T_DQ + lane_off + cc * 32, v);
         tmem_wait_ld();
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          atomicAdd(reinterpret_cast<float4*>(dst + cc * 32 + e),
-                    make_float4(__uint_as_float(v[e]) * a.scale, __uint_as_float(v[e + 1]) * a.scale,
-                                __uint_as_float(v[e + 2]) * a.scale, __uint_as_float(v[e + 3]) * a.scale));
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(stg + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(v[4 * u]) * a.scale, __uint_as_float(v[4 * u + 1]) * a.scale,
+                          __uint_as_float(v[4 * u + 2]) * a.scale, __uint_as_float(v[4 * u + 3]) * a.scale);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tm_dq, stg, h * D + cc * 32, qrow0);
+          bulk_commit();
+        }
       }
       tc_fence_before();
       mbar_arrive(dq_free);
@@ -628,10 +645,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* lse = sLD + st * 256;
       const float* dlt = lse + 128;
       const bool diag = (i == 0);
-      uint8_t* pt_row = sPT + c * 128;
-      uint8_t* ds_row = sDS + c * 128;
+      uint8_t* pt_row = sPT + half * 16384 + c * 128;
+      uint8_t* ds_row = sDS + half * 16384 + c * 128;
 #pragma unroll
-      for (int cc = 0; cc < BM / 32; ++cc) {
+      for (int k2 = 0; k2 < 2; ++k2) {
+        const int cc = half * 2 + k2;            // 32-column chunk of the 128 query columns
         uint32_t sv[32], dv[32];
         tmem_ld_32x32b_x32(tmem + C::T_ST + lane_off + cc * 32, sv);
         tmem_ld_32x32b_x32(tmem + C::T_DPT + lane_off + cc * 32, dv);
@@ -649,12 +667,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           pp[e >> 1] = pack_bf16x2(p0, p1);
           dd[e >> 1] = pack_bf16x2(d0, d1);
         }
-        const int chunk = (cc >> 1) * 16384;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int sw = ((((cc & 1) * 4 + u) ^ (c & 7)) << 4);
-          *reinterpret_cast<uint4*>(pt_row + chunk + sw) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
-          *reinterpret_cast<uint4*>(ds_row + chunk + sw) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+          const int sw = (((k2 * 4 + u) ^ (c & 7)) << 4);
+          *reinterpret_cast<uint4*>(pt_row + sw) = make_uint4(pp[4 * u], pp[4 * u + 1], pp[4 * u + 2], pp[4 * u + 3]);
+          *reinterpret_cast<uint4*>(ds_row + sw) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
         }
       }
       tc_fence_before();
@@ -670,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __nv_bfloat16* dk = a.dqkv + row * a.ld_dqkv + a.k_col0 + h * D;
       __nv_bfloat16* dv = a.dqkv + row * a.ld_dqkv + a.v_col0 + h * D;
 #pragma unroll
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = half; cc < D / 32; cc += 2) {
         uint32_t kv[32], vv[32];
         tmem_ld_32x32b_x32(tmem + C::T_DK + lane_off + cc * 32, kv);
         tmem_ld_32x32b_x32(tmem + C::T_DV + lane_off + cc * 32, vv);
@@ -691,6 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -701,24 +720,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// delta[b, h, pos] = sum_d dO[row, h*D + d] * O[row, h*D + d]   (one warp per (row, head))
+// delta[b, h, pos] = sum_d dO[row, h*D + d] * O[row, h*D + d]
+// One thread per 8 elements (16 bytes); the D/8 threads of a (row, head) reduce with shuffles.
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
                                   long ld, int B, int S, int nh, int D, float* __restrict__ delta) {
-  const long w = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= (long)B * S * nh) return;
-  const long row = w / nh;
-  const int h = (int)(w % nh);
-  const __nv_bfloat16* a = dout + row * ld + h * D;
-  const __nv_bfloat16* o = out + row * ld + h * D;
+  const int g = D / 8;  // threads per (row, head): 8 or 16
+  const long tid = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  const long pair = tid / g;  // (row, head) index
+  const int part = (int)(tid % g);
+  const bool valid = pair < (long)B * S * nh;
   float acc = 0.f;
-  for (int c = lane * 2; c < D; c += 64) {
-    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + c));
-    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(o + c));
-    acc += x.x * y.x + x.y * y.y;
+  long row = 0;
+  int h = 0;
+  if (valid) {
+    row = pair / nh;
+    h = (int)(pair % nh);
+    const uint4 x = *reinterpret_cast<const uint4*>(dout + row * ld + h * D + part * 8);
+    const uint4 y = *reinterpret_cast<const uint4*>(out + row * ld + h * D + part * 8);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x);
+    const uint32_t* yw = reinterpret_cast<const uint32_t*>(&y);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 p = unpack_bf16x2(xw[e]), q = unpack_bf16x2(yw[e]);
+      acc += p.x * q.x + p.y * q.y;
+    }
   }
-  acc = warp_sum(acc);
-  if (lane == 0) {
+  for (int o = g / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (valid && part == 0) {
     const long b = row / S, pos = row % S;
     delta[((size_t)b * nh + h) * S + pos] = acc;
   }
@@ -750,8 +778,8 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
   const long rows = (long)B * S;
   // Delta = rowsum(dO * O)
   {
-    const long warps = rows * nh;
-    attn_delta_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream>>>(dout, out, ld_do, B, S, nh, d, delta);
+    const long threads = rows * nh * (d / 8);
+    attn_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(dout, out, ld_do, B, S, nh, d, delta);
   }
   cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * nh * d, stream);
   CUtensorMap tm_qkv, tm_do;
@@ -759,6 +787,9 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
   if (rc) return rc - 10;
   rc = make_tmap_bf16_2d(&tm_do, dout, rows, (long)nh * d, ld_do, 64, BM);
   if (rc) return rc - 20;
+  CUtensorMap tm_dq;
+  rc = make_tmap_f32_2d(&tm_dq, dq_acc, rows, (long)nh * d, (long)nh * d, 32, 32);
+  if (rc) return rc - 30;
   BwdArgs a;
   a.B = B;
   a.S = S;
@@ -783,7 +814,7 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<64>::SMEM);
       set = true;
     }
-    k<<<grid, kThreads, BwdCfg<64>::SMEM, stream>>>(tm_qkv, tm_do, a);
+    k<<<grid, kBwdThreads, BwdCfg<64>::SMEM, stream>>>(tm_qkv, tm_do, tm_dq, a);
   } else {
     auto k = flash_bwd_kernel<128>;
     static bool set = false;
@@ -791,7 +822,7 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<128>::SMEM);
       set = true;
     }
-    k<<<grid, kThreads, BwdCfg<128>::SMEM, stream>>>(tm_qkv, tm_do, a);
+    k<<<grid, kBwdThreads, BwdCfg<128>::SMEM, stream>>>(tm_qkv, tm_do, tm_dq, a);
   }
   const long n4 = rows * nh * d / 4;
   attn_dq_convert_kernel<<<(unsigned)std::min<long>((n4 + 255) / 256, (long)num_sms * 8), 256, 0, stream>>>(

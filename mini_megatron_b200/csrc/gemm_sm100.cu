@@ -438,6 +438,10 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, 
   return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_cols, box_rows);
 }
 
+int make_tmap_f32_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_cols, box_rows);
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                               const CUtensorMap& tx, const GemmArgs& args, int grid, cudaStream_t stream) {

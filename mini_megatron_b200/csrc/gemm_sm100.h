@@ -46,6 +46,7 @@ struct GemmProblem {
 
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols,
                       int box_rows);
+int make_tmap_f32_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
 int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream);
 int choose_bn(int M, int N, int num_sms);
 

@@ -75,8 +75,8 @@ template <int NV, bool FUSE_PARAM>
 __global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
                                                      const float* __restrict__ gamma, const float* __restrict__ dres,
-                                                     float* __restrict__ dx, float* __restrict__ part, int rows,
-                                                     int H) {
+                                                     float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
+                                                     float* __restrict__ part, int rows, int H) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -126,18 +126,37 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __rest
           o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
         }
         dxr[c] = o;
+        if (dx_bf16) {
+          uint2 ob;
+          ob.x = pack_bf16x2(o.x, o.y);
+          ob.y = pack_bf16x2(o.z, o.w);
+          reinterpret_cast<uint2*>(dx_bf16 + (size_t)r * H)[c] = ob;
+        }
       }
     }
   }
   if constexpr (FUSE_PARAM) {
-    float4* pg = reinterpret_cast<float4*>(part + (size_t)gw * 2 * H);
+    // reduce the 8 warps' partial sums in shared memory: one partial row per CTA
+    extern __shared__ float4 red[];  // [8 warps][2 * nvec]
+    const int wid = threadIdx.x >> 5;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
-        pg[c] = dg[i];
-        pg[nvec + c] = db[i];
+        red[wid * 2 * nvec + c] = dg[i];
+        red[wid * 2 * nvec + nvec + c] = db[i];
       }
+    }
+    __syncthreads();
+    float4* pg = reinterpret_cast<float4*>(part + (size_t)blockIdx.x * 2 * H);
+    for (int c = threadIdx.x; c < 2 * nvec; c += blockDim.x) {
+      float4 acc = red[c];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) {
+        const float4 t = red[w * 2 * nvec + c];
+        acc.x += t.x; acc.y += t.y; acc.z += t.z; acc.w += t.w;
+      }
+      pg[c] = acc;
     }
   }
 }
@@ -196,26 +215,42 @@ int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bf
 // Number of fp32 [2H] partial rows the backward needs as scratch.
 int layernorm_bwd_parts(int rows, int H, int num_sms) {
   const int nv = (H / 4 + 31) / 32;
-  if (nv <= 8) return 8 * std::min(2 * num_sms, std::max(1, (rows + 7) / 8));  // one per warp
+  if (nv <= 8) return std::min(4 * num_sms, std::max(1, (rows + 7) / 8));  // one per CTA of 8 warps
   return std::min(4 * num_sms, std::max(1, rows / 16));                          // one per band
 }
 
 int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
                   const float* dres, float* dx, float* part, float* dgamma, float* dbeta, int rows, int H,
                   int nparts, cudaStream_t s) {
+  return layernorm_bwd2(dy, x, mean, rstd, gamma, dres, dx, nullptr, part, dgamma, dbeta, rows, H, nparts, s);
+}
+
+int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
+                   const float* dres, float* dx, __nv_bfloat16* dx_bf16, float* part, float* dgamma, float* dbeta,
+                   int rows, int H, int nparts, cudaStream_t s) {
   if (H % 4 != 0 || H > 4096) return -1;
   const int nv = (H / 4 + 31) / 32;
   if (nv <= 8) {
-    const int blocks = nparts / 8;
-#define LN_BWD(NVV) ln_bwd_kernel<NVV, true><<<blocks, 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, part, rows, H)
+    const int blocks = nparts;  // one partial row per CTA
+    const int smem = 8 * 2 * (H / 4) * 16;
+#define LN_BWD(NVV)                                                                                      \
+  do {                                                                                                   \
+    if (smem > 48 * 1024)                                                                                \
+      cudaFuncSetAttribute(ln_bwd_kernel<NVV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    ln_bwd_kernel<NVV, true><<<blocks, 256, smem, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16, part, rows, H); \
+  } while (0)
     if (nv <= 2) LN_BWD(2);
     else if (nv <= 6) LN_BWD(6);
     else LN_BWD(8);
 #undef LN_BWD
   } else {
     const int blocks = std::max(1, (rows * 32 + 255) / 256);
-    if (nv <= 16) ln_bwd_kernel<16, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, rows, H);
-    else ln_bwd_kernel<32, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, rows, H);
+    if (nv <= 16)
+      ln_bwd_kernel<16, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
+                                                                         nullptr, rows, H);
+    else
+      ln_bwd_kernel<32, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
+                                                                         nullptr, rows, H);
     const int rows_per_band = (rows + nparts - 1) / nparts;
     dim3 grid(nparts, (H + 255) / 256);
     ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);

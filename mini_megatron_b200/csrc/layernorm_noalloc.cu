@@ -57,9 +57,7 @@ extern "C" __attribute__((visibility("default"))) int mmb_layernorm_bwd_noalloc(
   const long cap = (long)MMB_LN_NOALLOC_SCRATCH_FLOATS / (2L * H);
   int nparts = mmb::layernorm_bwd_parts(rows, H, s->num_sms);
   if (nparts > cap) nparts = (int)cap;
-  const int nv = (H / 4 + 31) / 32;
-  if (nv <= 8) nparts -= nparts % 8;  // the fused row pass uses one partial row per warp, 8 warps per CTA
-  if (nparts < (nv <= 8 ? 8 : 1)) return MMB_LN_NOALLOC_EBADSHAPE;
+  if (nparts < 1) return MMB_LN_NOALLOC_EBADSHAPE;
   const int rc = mmb::layernorm_bwd(static_cast<const __nv_bfloat16*>(dy_bf16), x, mean, rstd, gamma, dres, dx,
                                     s->scratch, dgamma, dbeta, rows, H, nparts, stream);
   return rc;

@@ -17,6 +17,10 @@ int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, co
                   const float* dres, float* dx, float* part, float* dgamma, float* dbeta, int rows, int H,
                   int nparts, cudaStream_t s);
 
+int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
+                   const float* dres, float* dx, __nv_bfloat16* dx_bf16, float* part, float* dgamma, float* dbeta,
+                   int rows, int H, int nparts, cudaStream_t s);
+
 int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
                  float* out_max, float* out_sum, float* out_tgt, cudaStream_t s);
 int ce_bwd(__nv_bfloat16* logits, long ld, int n_cols, const long* labels, long vocab_start, int n_valid, int rows,

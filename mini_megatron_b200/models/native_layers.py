@@ -50,11 +50,20 @@ def _ln_fwd(x2, ln):
     return y, mean, rstd
 
 
-def _ln_bwd(dy, x2, mean, rstd, ln, dres=None):
+def _ln_bwd(dy, x2, mean, rstd, ln, dres=None, want_bf16=False):
+    """LayerNorm backward; with ``want_bf16`` the same kernel also writes a bf16 copy of dx."""
     dx = torch.empty_like(x2)
+    dxb = torch.empty(x2.shape, device=x2.device, dtype=torch.bfloat16) if want_bf16 else None
     native().layernorm_bwd(dy.contiguous(), x2, mean, rstd, ln.weight.detach(), dres, dx, grad_target(ln.weight),
-                           grad_target(ln.bias))
+                           grad_target(ln.bias), dxb)
+    if want_bf16:
+        dx._mmb_bf16 = dxb  # travels with the residual-stream gradient to the next layer's backward
     return dx
+
+
+def _bf16_of(t):
+    b = getattr(t, "_mmb_bf16", None)
+    return b if b is not None else t.to(torch.bfloat16)
 
 
 def _gather_seq(t2, B, group):
@@ -104,7 +113,7 @@ def _layer_backward(dout, saved, layer, B, S, group, sp):
     t = _world(group)
     (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, gelu_grad, act) = saved
     # ---- MLP
-    g = dout.to(torch.bfloat16)
+    g = _bf16_of(dout)
     g_full = _gather_seq(g, B, group) if sp else g
     w2, w1 = mlp.fc2.weight, mlp.fc1.weight
     d_pre = linear_dgrad(g_full, bf16_weight(w2), epi=EPI_DGELU, aux=gelu_grad)
@@ -113,9 +122,9 @@ def _layer_backward(dout, saved, layer, B, S, group, sp):
     linear_wgrad(d_pre, ln2_full, grad_target(w1))
     if t > 1:
         d_ln2 = _reduce(d_ln2, B, group, sp)
-    dx1 = _ln_bwd(d_ln2, x1, m2, r2, layer.ln2, dres=dout)
+    dx1 = _ln_bwd(d_ln2, x1, m2, r2, layer.ln2, dres=dout, want_bf16=True)
     # ---- attention
-    g = dx1.to(torch.bfloat16)
+    g = dx1._mmb_bf16
     g_full = _gather_seq(g, B, group) if sp else g
     wo, wqkv = attn.o.weight, attn.qkv.weight
     d_ctx = linear_dgrad(g_full, bf16_weight(wo))
@@ -125,7 +134,7 @@ def _layer_backward(dout, saved, layer, B, S, group, sp):
     linear_wgrad(dqkv, ln1_full, grad_target(wqkv))
     if t > 1:
         d_ln1 = _reduce(d_ln1, B, group, sp)
-    return _ln_bwd(d_ln1, x2, m1, r1, layer.ln1, dres=dx1)
+    return _ln_bwd(d_ln1, x2, m1, r1, layer.ln1, dres=dx1, want_bf16=True)
 
 
 class DecoderLayerFn(torch.autograd.Function):
@@ -158,10 +167,14 @@ class DecoderLayerFn(torch.autograd.Function):
             _, saved = _layer_forward(x2, ctx.layer, ctx.B, ctx.S, ctx.group, ctx.sp)
         else:
             saved = ctx.saved_tensors
+        if getattr(dout, "_mmb_bf16", None) is not None:
+            d2._mmb_bf16 = dout._mmb_bf16.view(-1, H)
         dx = _layer_backward(d2, saved, ctx.layer, ctx.B, ctx.S, ctx.group, ctx.sp)
         for hook in getattr(ctx.layer, "_mmb_grad_ready_hooks", ()):
             hook()
-        return (dx.view(B, S_l, H), None, None, None, None) + (None,) * ctx.n_params
+        out = dx.view(B, S_l, H)
+        out._mmb_bf16 = dx._mmb_bf16.view(B, S_l, H)
+        return (out, None, None, None, None) + (None,) * ctx.n_params
 
 
 class EmbeddingFn(torch.autograd.Function):
@@ -251,5 +264,7 @@ class HeadLossFn(torch.autograd.Function):
         linear_wgrad(logits, ln_full, grad_target(w))
         if _world(ctx.group) > 1:
             d_ln = _reduce(d_ln, ctx.B, ctx.group, ctx.sp)
-        dx = _ln_bwd(d_ln, x2, m, r, ctx.ln_f)
-        return (dx.view(ctx.x_shape), None, None, None, None, None, None, None) + (None,) * ctx.n_params
+        dx = _ln_bwd(d_ln, x2, m, r, ctx.ln_f, want_bf16=True)
+        out = dx.view(ctx.x_shape)
+        out._mmb_bf16 = dx._mmb_bf16.view(ctx.x_shape)
+        return (out, None, None, None, None, None, None, None) + (None,) * ctx.n_params
