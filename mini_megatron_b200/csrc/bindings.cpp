@@ -371,6 +371,147 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
   MMB_CHECK_RC(mmb::dp_rs_adamw_ag(P, s, cur_stream()), "dp_rs_adamw_ag");
 }
 
+// ----------------------------------------------------------------- fused tensor parallel
+// push = (dst_ptrs[world], flag_ptrs[world], rank, epoch, S, Sl, ld, counter tensor)
+mmb::AgPush make_push(const std::vector<int64_t>& dst, const std::vector<int64_t>& flags, int64_t rank,
+                      int64_t epoch, int64_t S, int64_t Sl, int64_t ld, Tensor& counter) {
+  TORCH_CHECK(dst.size() == flags.size() && dst.size() >= 1 && dst.size() <= 8, "push: 1..8 ranks");
+  mmb::AgPush P{};
+  P.world = (int)dst.size();
+  P.rank = (int)rank;
+  for (size_t i = 0; i < dst.size(); ++i) {
+    P.dst[i] = reinterpret_cast<void*>(dst[i]);
+    P.flags[i] = reinterpret_cast<int*>(flags[i]);
+  }
+  P.ld = ld;
+  P.S = (int)S;
+  P.Sl = (int)Sl;
+  P.epoch = (int)epoch;
+  P.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
+  return P;
+}
+
+void layernorm_fwd_push(const Tensor& x, const Tensor& gamma, const Tensor& beta, Tensor& mean, Tensor& rstd,
+                        double eps, const std::vector<int64_t>& dst, const std::vector<int64_t>& flags, int64_t rank,
+                        int64_t epoch, int64_t S, int64_t Sl, Tensor& counter) {
+  check_f32(x, "x");
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, S, Sl, H, counter);
+  MMB_CHECK_RC(mmb::layernorm_fwd_push(x.data_ptr<float>(), gamma.data_ptr<float>(), beta.data_ptr<float>(),
+                                       mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, H, (float)eps, P,
+                                       num_sms(), cur_stream()),
+               "layernorm_fwd_push");
+}
+
+void layernorm_bwd_push(const Tensor& dy, const Tensor& x, const Tensor& mean, const Tensor& rstd,
+                        const Tensor& gamma, const c10::optional<Tensor>& dres, Tensor& dx, Tensor& dgamma,
+                        Tensor& dbeta, const std::vector<int64_t>& dst, const std::vector<int64_t>& flags,
+                        int64_t rank, int64_t epoch, int64_t S, int64_t Sl, Tensor& counter) {
+  check_bf16(dy, "dy");
+  check_f32(x, "x");
+  check_f32(dx, "dx");
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  const int nparts = mmb::layernorm_bwd_parts(rows, H, num_sms());
+  Tensor part = at::empty({nparts, 2 * H}, x.options());
+  const float* dr = dres.has_value() ? dres->data_ptr<float>() : nullptr;
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, S, Sl, H, counter);
+  MMB_CHECK_RC(mmb::layernorm_bwd_push(reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), x.data_ptr<float>(),
+                                       mean.data_ptr<float>(), rstd.data_ptr<float>(), gamma.data_ptr<float>(), dr,
+                                       dx.data_ptr<float>(), part.data_ptr<float>(), dgamma.data_ptr<float>(),
+                                       dbeta.data_ptr<float>(), rows, H, nparts, P, cur_stream()),
+               "layernorm_bwd_push");
+}
+
+void tp_ag_push(const Tensor& src, const std::vector<int64_t>& dst, const std::vector<int64_t>& flags, int64_t rank,
+                int64_t epoch, int64_t S, int64_t Sl, Tensor& counter) {
+  check_bf16(src, "src");
+  const int H = (int)src.size(-1);
+  const int rows = (int)(src.numel() / H);
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, S, Sl, H, counter);
+  MMB_CHECK_RC(mmb::tp_ag_push(reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), rows, H, P, num_sms(),
+                               cur_stream()),
+               "tp_ag_push");
+}
+
+// out = resid + sum of `world` bf16 slots [rows_l, H] (slot s at slots_ptr + s*slot_stride elements)
+void tp_rs_reduce(int64_t slots_ptr, int64_t slot_stride, int64_t world, int64_t flags_ptr, int64_t epoch,
+                  const c10::optional<Tensor>& resid, const c10::optional<Tensor>& out,
+                  const c10::optional<Tensor>& out_bf16, int64_t n) {
+  const float* r = resid.has_value() ? resid->data_ptr<float>() : nullptr;
+  float* o = out.has_value() ? out->data_ptr<float>() : nullptr;
+  __nv_bfloat16* ob = out_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
+  MMB_CHECK_RC(mmb::tp_rs_reduce(reinterpret_cast<const __nv_bfloat16*>(slots_ptr), slot_stride, (int)world,
+                                 reinterpret_cast<const int*>(flags_ptr), (int)epoch, r, o, ob, n, error_word(),
+                                 num_sms(), cur_stream()),
+               "tp_rs_reduce");
+}
+
+// GEMM with the TP collectives fused: optional all-gather wait on A rows and/or
+// reduce-scatter push epilogue (epi == EPI_PUSH_BF16, D unused).
+void gemm_tp(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const c10::optional<Tensor>& D, int64_t epi,
+             const c10::optional<Tensor>& aux, int64_t ag_flags, int64_t ag_epoch, int64_t S, int64_t Sl,
+             const std::vector<int64_t>& push_dst, const std::vector<int64_t>& push_flags, int64_t rank,
+             int64_t push_epoch, const c10::optional<Tensor>& push_counter, int64_t N_out) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1, "gemm_tp operands must be row-major");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  TORCH_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "gemm_tp: K mismatch");
+  TORCH_CHECK(N % 8 == 0 && N == N_out, "gemm_tp: N");
+  mmb::GemmProblem p{};
+  p.A = A.data_ptr();
+  p.lda = A.stride(0);
+  p.a_mn = a_mn;
+  p.B = B.data_ptr();
+  p.ldb = B.stride(0);
+  p.b_mn = b_mn;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.num_sms = num_sms();
+  p.allow_split = false;
+  p.args.epi = (int)epi;
+  p.args.alpha = 1.f;
+  p.args.err = error_word();
+  if (ag_flags != 0) {
+    TORCH_CHECK(Sl % 128 == 0 && S % Sl == 0, "gemm_tp: all-gather shards must be multiples of 128 rows");
+    p.args.ag_flags = reinterpret_cast<const int*>(ag_flags);
+    p.args.ag_epoch = (int)ag_epoch;
+    p.args.ag_S = (int)S;
+    p.args.ag_Sl = (int)Sl;
+  }
+  if (epi == mmb::EPI_PUSH_BF16) {
+    TORCH_CHECK(push_dst.size() == push_flags.size() && push_dst.size() >= 1 && push_dst.size() <= 8, "push ranks");
+    TORCH_CHECK(push_counter.has_value(), "push needs a counter");
+    p.args.ldd = N;
+    p.args.push_world = (int)push_dst.size();
+    p.args.push_rank = (int)rank;
+    p.args.push_epoch = (int)push_epoch;
+    p.args.push_S = (int)S;
+    p.args.push_Sl = (int)Sl;
+    for (size_t i = 0; i < push_dst.size(); ++i) {
+      p.args.push_dst[i] = reinterpret_cast<void*>(push_dst[i]);
+      p.args.push_flags[i] = reinterpret_cast<int*>(push_flags[i]);
+    }
+    p.args.push_counter = reinterpret_cast<unsigned*>(push_counter->data_ptr<int>());
+    p.args.D = p.args.push_dst[rank];
+  } else {
+    TORCH_CHECK(D.has_value(), "gemm_tp: D required");
+    p.args.D = D->data_ptr();
+    p.args.ldd = D->stride(0);
+    if (aux.has_value()) {
+      p.args.aux = aux->data_ptr();
+      p.args.ld_aux = aux->stride(0);
+    }
+  }
+  const int rc = mmb::gemm_bf16_launch(p, cur_stream());
+  TORCH_CHECK(rc == 0, "gemm_tp launch failed, code ", rc);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -399,6 +540,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("dp_rs_adamw_ag", &dp_rs_adamw_ag);
   m.def("dp_signal_pad_bytes", &mmb::dp_signal_pad_bytes);
+  m.def("layernorm_fwd_push", &layernorm_fwd_push);
+  m.def("layernorm_bwd_push", &layernorm_bwd_push);
+  m.def("tp_ag_push", &tp_ag_push);
+  m.def("tp_rs_reduce", &tp_rs_reduce);
+  m.def("gemm_tp", &gemm_tp);
+  m.attr("EPI_PUSH_BF16") = (int)mmb::EPI_PUSH_BF16;
   m.def("num_sms", &num_sms);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);

@@ -1,0 +1,103 @@
+// Tensor-parallel collectives fused with the kernels around them (sequence-
+// parallel dataflow over NVLink peer memory).
+//
+// The reference all-reduces Row-parallel outputs and Column-parallel input
+// gradients with NCCL (comm/all_reduce.py:5-43) and keeps a sequence-parallel
+// module that is not wired (comm/sequence_parallel.py).  Here, with
+// sequence parallelism, every activation between TP GEMMs is sharded along
+// the sequence, and the two collectives are folded into the kernels that
+// produce / consume the data:
+//
+//   all-gather      the producer of a sequence shard (LayerNorm forward, or
+//                   LayerNorm backward for gradients; layernorm.cu) writes
+//                   each bf16 row straight into every TP rank's gathered
+//                   buffer; the next Column GEMM's TMA producer waits per
+//                   source rank for that rank's flag before loading its rows
+//                   (gemm_sm100.cu), so local rows start immediately;
+//   reduce-scatter  the Row GEMM's epilogue pushes each bf16 partial output
+//                   tile into the owning rank's per-source slot
+//                   (gemm_sm100.cu, EPI_PUSH_BF16); `tp_rs_reduce` below waits
+//                   for every source and sums the slots (plus the residual).
+//
+// Flags hold monotonically increasing epochs (one counter per collective kind,
+// advanced identically on every rank); every wait is bounded (peer.cuh).
+#include "common.cuh"
+#include "ops.h"
+#include "peer.cuh"
+
+#include <algorithm>
+
+namespace mmb {
+
+// out[r] = (resid ? resid[r] : 0) + sum_src slot[src][r]   over rows_l x H,
+// after every source rank's flag reached `epoch`.  Outputs fp32 and/or bf16.
+__global__ void __launch_bounds__(256) tp_rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, long slot_stride,
+                                                           int world, const int* __restrict__ flags, int epoch,
+                                                           const float* __restrict__ resid, float* __restrict__ out,
+                                                           __nv_bfloat16* __restrict__ out_bf16, long n, int* err) {
+  if (!cta_wait_flags(flags, world, epoch, err)) return;
+  const long n8 = n >> 3;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    float acc[8];
+    if (resid) {
+      const float4 a = reinterpret_cast<const float4*>(resid)[2 * i];
+      const float4 b = reinterpret_cast<const float4*>(resid)[2 * i + 1];
+      acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w; acc[4] = b.x; acc[5] = b.y; acc[6] = b.z; acc[7] = b.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    }
+    for (int src = 0; src < world; ++src) {
+      const uint4 u = reinterpret_cast<const uint4*>(slots + src * slot_stride)[i];
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(w[e]);
+        acc[2 * e] += f.x;
+        acc[2 * e + 1] += f.y;
+      }
+    }
+    if (out) {
+      reinterpret_cast<float4*>(out)[2 * i] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(out)[2 * i + 1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+    if (out_bf16)
+      reinterpret_cast<uint4*>(out_bf16)[i] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+  }
+}
+
+// Stand-alone all-gather push of a local bf16 shard (used where the producer
+// kernel is not one of ours, e.g. a gradient handed in by autograd).
+__global__ void __launch_bounds__(256) tp_ag_push_kernel(const __nv_bfloat16* __restrict__ src, int rows, int H,
+                                                         const AgPush P) {
+  const int units = H / 8;
+  const long n = (long)rows * units;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / units), u = (int)(i % units);
+    const uint4 v = reinterpret_cast<const uint4*>(src + (size_t)r * H)[u];
+    const long grow = (long)(r / P.Sl) * P.S + (long)P.rank * P.Sl + r % P.Sl;
+    for (int p = 0; p < P.world; ++p)
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(P.dst[p]) + grow * P.ld)[u] = v;
+  }
+  grid_done_signal(P.flags, P.world, P.rank, P.epoch, P.counter);
+}
+
+int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
+                 const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
+                 cudaStream_t s) {
+  if (n % 8 != 0 || world < 1 || world > 8 || slot_stride % 8 != 0) return -1;
+  const int blocks = (int)std::max<long>(1, std::min<long>((n / 8 + 255) / 256, (long)num_sms * 4));
+  tp_rs_reduce_kernel<<<blocks, 256, 0, s>>>(slots, slot_stride, world, flags, epoch, resid, out, out_bf16, n, err);
+  return (int)cudaGetLastError();
+}
+
+int tp_ag_push(const __nv_bfloat16* src, int rows, int H, const AgPush& push, int num_sms, cudaStream_t s) {
+  if (H % 8 != 0 || push.world < 1 || push.world > 8) return -1;
+  const long n = (long)rows * (H / 8);
+  const int blocks = (int)std::max<long>(1, std::min<long>((n + 255) / 256, (long)num_sms * 4));
+  tp_ag_push_kernel<<<blocks, 256, 0, s>>>(src, rows, H, push);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace mmb

@@ -22,6 +22,7 @@
 // overlap the main loop of tile i+1.  Tiles are 128 x BN x 64.
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "peer.cuh"
 
 #include <algorithm>
 #include <cstdio>
@@ -148,10 +149,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_par = 0;
       bool ok = true;
+      uint32_t ag_ready = 0;  // source ranks whose rows are known to have arrived
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
         tile_coords(t / splits, mtiles, ntiles, tm, tn);
         const int m0 = tm * BM, n0 = tn * BN;
+        if (args.ag_flags != nullptr) {
+          const int src = (m0 % args.ag_S) / args.ag_Sl;
+          if (!((ag_ready >> src) & 1u)) {
+            if (!wait_flag_ge(args.ag_flags + src, args.ag_epoch, args.err)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            ag_ready |= 1u << src;
+          }
+        }
         const int kb_lo = (t % splits) * kb_per_split;
         const int kb_hi = min(kblocks_total, kb_lo + kb_per_split);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
@@ -253,7 +266,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // chunks (128 bytes per row either way).  Warps w and w+4 share a TMEM lane
     // quarter and take alternate chunks, so two warps per scheduler run the
     // epilogue math.
-    constexpr bool OUT_BF16 = (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU);
+    constexpr bool OUT_BF16 = (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU || EPI == EPI_PUSH_BF16);
     constexpr int W = OUT_BF16 ? 64 : 32;
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;   // which alternate chunks this warp takes
@@ -304,7 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // the previous store from this warp's stage must have finished reading it
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
-        if constexpr (EPI == EPI_BF16) {
+        if constexpr (EPI == EPI_BF16 || EPI == EPI_PUSH_BF16) {
 #pragma unroll
           for (int u = 0; u < 8; ++u)
             *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
@@ -371,6 +384,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             *reinterpret_cast<float4*>(stage_unit(stg, lane, u)) =
                 make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
         }
+        if constexpr (EPI == EPI_PUSH_BF16) {
+          // reduce-scatter: coalesced NVLink stores of the staged 32-row chunk into the owner's slot
+          __syncwarp();
+          const int owner = (r0 % args.push_S) / args.push_Sl;
+          const long lr0 = (long)(r0 / args.push_S) * args.push_Sl + (r0 % args.push_S) - owner * args.push_Sl;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(args.push_dst[owner]) + (lr0 * args.ldd + col0) * 2;
+          const int unit = lane & 7;
+#pragma unroll
+          for (int itr = 0; itr < 8; ++itr) {
+            const int row = itr * 4 + (lane >> 3);
+            if (row < rows_valid && unit * 16 < colb_valid)
+              *reinterpret_cast<uint4*>(dst + (size_t)row * args.ldd * 2 + unit * 16) =
+                  *reinterpret_cast<const uint4*>(stage_unit(stg, row, unit));
+          }
+          __syncwarp();
+          continue;
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -391,6 +421,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (EPI == EPI_PUSH_BF16) {
+    // every tile of this rank has been pushed: the last CTA tells each owner
+    if (!*abort_flag)
+      grid_done_signal(args.push_flags, args.push_world, args.push_rank, args.push_epoch, args.push_counter);
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
@@ -468,6 +503,7 @@ static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, co
     case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, td, tx, args, grid, s);
     case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, td, tx, args, grid, s);
     case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC>(ta, tb, td, tx, args, grid, s);
+    case EPI_PUSH_BF16: return launch_one<BN, A_MN, B_MN, EPI_PUSH_BF16>(ta, tb, td, tx, args, grid, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -551,7 +587,14 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   // output (and GELU pre-activation) maps for the TMA-store epilogue
   CUtensorMap td, tx;
   const bool out_bf16 = (args.epi == EPI_BF16 || args.epi == EPI_GELU || args.epi == EPI_DGELU);
-  if (out_bf16) rc = make_tmap_2d(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.D, p.M, p.N, args.ldd, 64, 32);
+  if (args.epi == EPI_PUSH_BF16) {
+    // the epilogue writes peer slots with plain stores; this map only keeps the launch well-formed
+    if (args.push_world < 1 || args.push_world > 8 || args.push_Sl % 32 != 0 || args.push_S % args.push_Sl != 0)
+      return -60;
+    rc = make_tmap_2d(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.push_dst[args.push_rank], 32, p.N, args.ldd, 64,
+                      32);
+  } else if (out_bf16)
+    rc = make_tmap_2d(&td, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, args.D, p.M, p.N, args.ldd, 64, 32);
   else rc = make_tmap_2d(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, args.D, p.M, p.N, args.ldd, 32, 32);
   if (rc) return rc - 40;
   if (args.epi == EPI_GELU) {

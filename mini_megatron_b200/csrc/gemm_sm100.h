@@ -14,6 +14,7 @@ enum GemmEpilogue : int {
   EPI_RESID = 4,    // D(fp32)  = resid(fp32) + alpha*acc (resid may alias D)
   EPI_DGELU = 5,    // D(bf16)  = alpha*acc * aux(bf16)          (aux = gelu'(pre) from EPI_GELU)
   EPI_F32_ATOMIC = 6,  // D(fp32) += alpha*acc with atomics (split-K partial sums)
+  EPI_PUSH_BF16 = 7,   // bf16 tile -> owning TP rank's reduce-scatter slot (NVLink stores), then signal
 };
 
 struct GemmArgs {
@@ -28,6 +29,16 @@ struct GemmArgs {
   float alpha;
   int* err;     // device error word (bounded-wait timeouts)
   int splits;   // K splits (set by the launcher)
+  // all-gather consumer: rows of A from source rank o = (m % ag_S) / ag_Sl are
+  // loaded only after ag_flags[o] >= ag_epoch (nullptr: no waiting)
+  const int* ag_flags;
+  int ag_epoch, ag_S, ag_Sl;
+  // reduce-scatter producer (EPI_PUSH_BF16): row m goes to owner o = (m % push_S) / push_Sl,
+  // local row (m / push_S) * push_Sl + m % push_Sl of push_dst[o] (ld = ldd)
+  void* push_dst[8];
+  int* push_flags[8];
+  int push_world, push_rank, push_epoch, push_S, push_Sl;
+  unsigned* push_counter;
 };
 
 struct GemmProblem {

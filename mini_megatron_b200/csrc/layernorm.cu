@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "ops.h"
+#include "peer.cuh"
 
 namespace mmb {
 
@@ -69,14 +70,70 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
   }
 }
 
+// Forward with the tensor-parallel all-gather fused in: each warp normalises
+// rows of this rank's sequence shard and writes the bf16 row into EVERY TP
+// rank's gathered buffer (NVLink stores for the peers), then the last CTA
+// signals the peers that this rank's shard is complete.
+template <int NV>
+__global__ void __launch_bounds__(256) ln_fwd_push_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                          const float* __restrict__ beta, float* __restrict__ mean_out,
+                                                          float* __restrict__ rstd_out, int rows, int H, float eps,
+                                                          const AgPush P) {
+  const int lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  const int nvec = H >> 2;
+  const float4* g4 = reinterpret_cast<const float4*>(gamma);
+  const float4* b4 = reinterpret_cast<const float4*>(beta);
+  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nwarps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * H);
+    float4 v[NV];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      v[i] = (c < nvec) ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      s += v[i].x + v[i].y + v[i].z + v[i].w;
+    }
+    const float mean = warp_sum(s) / H;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        const float a = v[i].x - mean, b = v[i].y - mean, cc = v[i].z - mean, d = v[i].w - mean;
+        ss += a * a + b * b + cc * cc + d * d;
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(ss) / H + eps);
+    const long grow = (long)(row / P.Sl) * P.S + (long)P.rank * P.Sl + row % P.Sl;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        const float4 g = g4[c], b = b4[c];
+        uint2 o;
+        o.x = pack_bf16x2((v[i].x - mean) * rstd * g.x + b.x, (v[i].y - mean) * rstd * g.y + b.y);
+        o.y = pack_bf16x2((v[i].z - mean) * rstd * g.z + b.z, (v[i].w - mean) * rstd * g.w + b.w);
+        for (int p = 0; p < P.world; ++p)
+          reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.dst[p]) + grow * P.ld)[c] = o;
+      }
+    }
+    if (lane == 0) {
+      mean_out[row] = mean;
+      rstd_out[row] = rstd;
+    }
+  }
+  grid_done_signal(P.flags, P.world, P.rank, P.epoch, P.counter);
+}
+
 // Row pass.  With FUSE_PARAM, each warp also accumulates dgamma/dbeta over the
 // rows it visits and writes them to part[global_warp][0:2H].
-template <int NV, bool FUSE_PARAM>
+template <int NV, bool FUSE_PARAM, bool PUSH = false>
 __global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
                                                      const float* __restrict__ gamma, const float* __restrict__ dres,
                                                      float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
-                                                     float* __restrict__ part, int rows, int H) {
+                                                     float* __restrict__ part, int rows, int H, const AgPush P = AgPush{}) {
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -126,11 +183,17 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __rest
           o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
         }
         dxr[c] = o;
-        if (dx_bf16) {
+        if (dx_bf16 || PUSH) {
           uint2 ob;
           ob.x = pack_bf16x2(o.x, o.y);
           ob.y = pack_bf16x2(o.z, o.w);
-          reinterpret_cast<uint2*>(dx_bf16 + (size_t)r * H)[c] = ob;
+          if (dx_bf16) reinterpret_cast<uint2*>(dx_bf16 + (size_t)r * H)[c] = ob;
+          if constexpr (PUSH) {
+            // all-gather fused in: the bf16 gradient row goes to every TP rank's gathered buffer
+            const long grow = (long)(r / P.Sl) * P.S + (long)P.rank * P.Sl + r % P.Sl;
+            for (int p = 0; p < P.world; ++p)
+              reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(P.dst[p]) + grow * P.ld)[c] = ob;
+          }
         }
       }
     }
@@ -159,6 +222,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __rest
       pg[c] = acc;
     }
   }
+  if constexpr (PUSH) grid_done_signal(P.flags, P.world, P.rank, P.epoch, P.counter);
 }
 
 // Column pass for wide rows: CTA (band, column block of 256 columns); each
@@ -251,6 +315,56 @@ int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, c
     else
       ln_bwd_kernel<32, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
                                                                          nullptr, rows, H);
+    const int rows_per_band = (rows + nparts - 1) / nparts;
+    dim3 grid(nparts, (H + 255) / 256);
+    ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);
+  }
+  dim3 fold((2 * H + 255) / 256, std::min(kLnFoldGroups, nparts));
+  ln_param_grad_kernel<<<fold, 256, 0, s>>>(part, nparts, H, dgamma, dbeta);
+  return (int)cudaGetLastError();
+}
+
+int layernorm_fwd_push(const float* x, const float* gamma, const float* beta, float* mean, float* rstd, int rows,
+                       int H, float eps, const AgPush& push, int num_sms, cudaStream_t s) {
+  if (H % 4 != 0 || H > 4096 || push.world < 1 || push.world > 8 || push.Sl <= 0) return -1;
+  const int blocks = std::max(1, std::min((rows + 7) / 8, 4 * num_sms));
+  const int nv = (H / 4 + 31) / 32;
+#define LN_FWDP(NVV) ln_fwd_push_kernel<NVV><<<blocks, 256, 0, s>>>(x, gamma, beta, mean, rstd, rows, H, eps, push)
+  if (nv <= 2) LN_FWDP(2);
+  else if (nv <= 6) LN_FWDP(6);
+  else if (nv <= 8) LN_FWDP(8);
+  else if (nv <= 16) LN_FWDP(16);
+  else LN_FWDP(32);
+#undef LN_FWDP
+  return (int)cudaGetLastError();
+}
+
+int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd,
+                       const float* gamma, const float* dres, float* dx, float* part, float* dgamma, float* dbeta,
+                       int rows, int H, int nparts, const AgPush& push, cudaStream_t s) {
+  if (H % 4 != 0 || H > 4096 || push.world < 1 || push.world > 8 || push.Sl <= 0) return -1;
+  const int nv = (H / 4 + 31) / 32;
+  if (nv <= 8) {
+    const int smem = 8 * 2 * (H / 4) * 16;
+#define LN_BWDP(NVV)                                                                                               \
+  do {                                                                                                             \
+    if (smem > 48 * 1024)                                                                                          \
+      cudaFuncSetAttribute(ln_bwd_kernel<NVV, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);     \
+    ln_bwd_kernel<NVV, true, true><<<nparts, 256, smem, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, part, rows, \
+                                                             H, push);                                              \
+  } while (0)
+    if (nv <= 2) LN_BWDP(2);
+    else if (nv <= 6) LN_BWDP(6);
+    else LN_BWDP(8);
+#undef LN_BWDP
+  } else {
+    const int blocks = std::min(std::max(1, (rows * 32 + 255) / 256), 1184);
+    if (nv <= 16)
+      ln_bwd_kernel<16, false, true><<<blocks, 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, nullptr, rows,
+                                                             H, push);
+    else
+      ln_bwd_kernel<32, false, true><<<blocks, 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, nullptr, rows,
+                                                             H, push);
     const int rows_per_band = (rows + nparts - 1) / nparts;
     dim3 grid(nparts, (H + 255) / 256);
     ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);

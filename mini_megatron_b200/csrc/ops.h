@@ -10,6 +10,20 @@
 
 namespace mmb {
 
+// All-gather push target for the fused tensor-parallel path: the producer of a
+// sequence-sharded bf16 activation writes each of its rows straight into every
+// TP rank's gathered buffer ([B*S, ld] bf16, peer pointers), then the last CTA
+// publishes `epoch` in slot [rank] of every rank's AG flag array.
+struct AgPush {
+  int world, rank;
+  void* dst[8];
+  long ld;
+  int S, Sl;           // local row r = b*Sl + s  ->  gathered row b*S + rank*Sl + s
+  int* flags[8];
+  int epoch;
+  unsigned* counter;   // local, zero-initialised completion counter
+};
+
 int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bfloat16* y, float* mean, float* rstd,
                   int rows, int H, float eps, cudaStream_t s);
 int layernorm_bwd_parts(int rows, int H, int num_sms);
@@ -20,6 +34,17 @@ int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, co
 int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,
                    const float* dres, float* dx, __nv_bfloat16* dx_bf16, float* part, float* dgamma, float* dbeta,
                    int rows, int H, int nparts, cudaStream_t s);
+
+int layernorm_fwd_push(const float* x, const float* gamma, const float* beta, float* mean, float* rstd, int rows,
+                       int H, float eps, const AgPush& push, int num_sms, cudaStream_t s);
+int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd,
+                       const float* gamma, const float* dres, float* dx, float* part, float* dgamma, float* dbeta,
+                       int rows, int H, int nparts, const AgPush& push, cudaStream_t s);
+
+int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
+                 const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
+                 cudaStream_t s);
+int tp_ag_push(const __nv_bfloat16* src, int rows, int H, const AgPush& push, int num_sms, cudaStream_t s);
 
 int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
                  float* out_max, float* out_sum, float* out_tgt, cudaStream_t s);

@@ -137,6 +137,52 @@ def _layer_backward(dout, saved, layer, B, S, group, sp):
     return _ln_bwd(d_ln1, x2, m1, r1, layer.ln1, dres=dx1, want_bf16=True)
 
 
+def _layer_forward_fused(x2, layer, B, S, ws):
+    """Sequence-parallel layer forward with the TP collectives fused into the kernels (parallel/fused_tp.py)."""
+    attn, mlp = layer.attn, layer.mlp
+    slot = layer._mmb_tp_slot
+    ln1_full, m1, r1, e1 = ws.ln_fwd_ag(x2, layer.ln1, 2 * slot)
+    qkv = torch.empty(ws.rows, attn.qkv.weight.shape[0], device=x2.device, dtype=torch.bfloat16)
+    ws.gemm_ag(ln1_full, e1, bf16_weight(attn.qkv.weight), False, qkv)
+    ctx_out, lse = flash_attn_fwd(qkv, B, S, attn.num_heads, attn.head_dim)
+    x1 = ws.rs_reduce(ws.gemm_rs(ctx_out, bf16_weight(attn.o.weight), False), resid=x2)
+    ln2_full, m2, r2, e2 = ws.ln_fwd_ag(x1, layer.ln2, 2 * slot + 1)
+    n_ffn = mlp.fc1.weight.shape[0]
+    act = torch.empty(ws.rows, n_ffn, device=x2.device, dtype=torch.bfloat16)
+    gelu_grad = torch.empty_like(act)
+    ws.gemm_ag(ln2_full, e2, bf16_weight(mlp.fc1.weight), False, act, epi=3, aux=gelu_grad)
+    out = ws.rs_reduce(ws.gemm_rs(act, bf16_weight(mlp.fc2.weight), False), resid=x1)
+    if ws.copy_saved:  # several microbatches in flight (pipeline): keep private copies for the wgrads
+        ln1_full, ln2_full = ln1_full.clone(), ln2_full.clone()
+    saved = (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, gelu_grad, act)
+    return out, saved
+
+
+def _layer_backward_fused(dout, saved, layer, B, S, ws):
+    attn, mlp = layer.attn, layer.mlp
+    (x2, m1, r1, ln1_full, qkv, ctx_out, lse, x1, m2, r2, ln2_full, gelu_grad, act) = saved
+    w2, w1, wo, wqkv = mlp.fc2.weight, mlp.fc1.weight, attn.o.weight, attn.qkv.weight
+    # ---- MLP: gathered output gradient (pushed by the producer of dout, or pushed here)
+    g_full, eg = ws.gather_grad(dout)
+    d_pre = torch.empty(ws.rows, w1.shape[0], device=dout.device, dtype=torch.bfloat16)
+    ws.gemm_ag(g_full, eg, bf16_weight(w2), True, d_pre, epi=EPI_DGELU, aux=gelu_grad)
+    linear_wgrad(g_full, act, grad_target(w2))
+    e_rs = ws.gemm_rs(d_pre, bf16_weight(w1), True)
+    linear_wgrad(d_pre, ln2_full, grad_target(w1))
+    d_ln2 = ws.rs_reduce(e_rs, out_bf16=True)
+    dx1 = ws.ln_bwd_ag(d_ln2, x1, m2, r2, layer.ln2, dout, grad_target)
+    # ---- attention
+    g_full, eg = dx1._mmb_gathered
+    d_ctx = torch.empty(ws.rows, wo.shape[1], device=dout.device, dtype=torch.bfloat16)
+    ws.gemm_ag(g_full, eg, bf16_weight(wo), True, d_ctx)
+    linear_wgrad(g_full, ctx_out, grad_target(wo))
+    dqkv = flash_attn_bwd(d_ctx, qkv, ctx_out, lse, B, S, attn.num_heads, attn.head_dim)
+    e_rs = ws.gemm_rs(dqkv, bf16_weight(wqkv), True)
+    linear_wgrad(dqkv, ln1_full, grad_target(wqkv))
+    d_ln1 = ws.rs_reduce(e_rs, out_bf16=True)
+    return ws.ln_bwd_ag(d_ln1, x2, m1, r1, layer.ln1, dx1, grad_target)
+
+
 class DecoderLayerFn(torch.autograd.Function):
     """x_out = x + MLP(LN2(x1)), x1 = x + Attn(LN1(x)) on the native kernels."""
 
@@ -148,7 +194,12 @@ class DecoderLayerFn(torch.autograd.Function):
         B, S_l, H = x.shape
         S = S_l * (_world(group) if sp else 1)
         x2 = x.reshape(-1, H).contiguous()
-        out, saved = _layer_forward(x2, layer, B, S, group, sp)
+        ws = getattr(layer, "_mmb_tp_ws", None) if sp else None
+        ctx.ws = ws
+        if ws is not None:
+            out, saved = _layer_forward_fused(x2, layer, B, S, ws)
+        else:
+            out, saved = _layer_forward(x2, layer, B, S, group, sp)
         ctx.layer, ctx.group, ctx.sp, ctx.B, ctx.S, ctx.recompute = layer, group, sp, B, S, recompute
         if recompute:
             ctx.save_for_backward(x2)
@@ -162,18 +213,30 @@ class DecoderLayerFn(torch.autograd.Function):
     def backward(ctx, dout):
         B, S_l, H = dout.shape
         d2 = dout.reshape(-1, H).contiguous()
+        ws = ctx.ws
         if ctx.recompute:
             (x2,) = ctx.saved_tensors
-            _, saved = _layer_forward(x2, ctx.layer, ctx.B, ctx.S, ctx.group, ctx.sp)
+            if ws is not None:
+                _, saved = _layer_forward_fused(x2, ctx.layer, ctx.B, ctx.S, ws)
+            else:
+                _, saved = _layer_forward(x2, ctx.layer, ctx.B, ctx.S, ctx.group, ctx.sp)
         else:
             saved = ctx.saved_tensors
         if getattr(dout, "_mmb_bf16", None) is not None:
             d2._mmb_bf16 = dout._mmb_bf16.view(-1, H)
-        dx = _layer_backward(d2, saved, ctx.layer, ctx.B, ctx.S, ctx.group, ctx.sp)
+        if getattr(dout, "_mmb_gathered", None) is not None:
+            d2._mmb_gathered = dout._mmb_gathered
+        if ws is not None:
+            dx = _layer_backward_fused(d2, saved, ctx.layer, ctx.B, ctx.S, ws)
+        else:
+            dx = _layer_backward(d2, saved, ctx.layer, ctx.B, ctx.S, ctx.group, ctx.sp)
         for hook in getattr(ctx.layer, "_mmb_grad_ready_hooks", ()):
             hook()
         out = dx.view(B, S_l, H)
-        out._mmb_bf16 = dx._mmb_bf16.view(B, S_l, H)
+        if getattr(dx, "_mmb_bf16", None) is not None:
+            out._mmb_bf16 = dx._mmb_bf16.view(B, S_l, H)
+        if getattr(dx, "_mmb_gathered", None) is not None:
+            out._mmb_gathered = dx._mmb_gathered
         return (out, None, None, None, None) + (None,) * ctx.n_params
 
 

@@ -1,0 +1,166 @@
+"""Fused tensor-parallel collectives (sequence-parallel dataflow over NVLink).
+
+With sequence parallelism every activation between tensor-parallel GEMMs is
+sharded along the sequence.  Instead of NCCL all-gathers / reduce-scatters,
+the kernels around each collective do the communication themselves:
+
+* **LayerNorm + all-gather** (``layernorm_fwd_push`` / ``layernorm_bwd_push``):
+  the kernel that produces a sequence shard writes every bf16 row straight into
+  each TP rank's gathered buffer and the last CTA raises this rank's flag;
+* **all-gather -> GEMM** (``gemm_tp`` with ``ag_flags``): the Column GEMM's TMA
+  producer waits, per source rank, for that rank's flag before loading its
+  rows, so tiles of already-arrived shards (the local one first) start at once;
+* **GEMM -> reduce-scatter** (``gemm_tp`` with ``EPI_PUSH_BF16``): the Row GEMM's
+  epilogue pushes each partial output tile into the owning rank's per-source
+  slot; ``tp_rs_reduce`` waits for all sources and sums the slots plus the
+  residual.
+
+``TPWorkspace`` owns the symmetric buffers of one model chunk: a signal pad
+(all-gather flags, reduce-scatter flags), two gathered buffers per decoder
+layer for the forward (kept for the weight gradients), two alternating
+gathered buffers for the backward, and the reduce-scatter slots.  Flags carry
+epochs from two counters (one per collective kind) that every rank advances
+in the same order; every device-side wait is bounded.
+
+Reference: the reference's TP all-reduces (comm/all_reduce.py:5-43) and its
+unwired sequence-parallel helpers (comm/sequence_parallel.py:8-53).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..comm.symmetric import SymmetricBuffer
+from ..ops import native
+
+
+class TPWorkspace:
+    SIG_BYTES = 4096  # int32 flags: [0:8] all-gather, [8:16] reduce-scatter
+
+    def __init__(self, tp_group, B: int, S: int, H: int, num_fwd_slots: int, copy_saved: bool = False):
+        self.group = tp_group
+        self.world = dist.get_world_size(tp_group)
+        self.rank = dist.get_rank(tp_group)
+        if self.world > 8:
+            raise ValueError("fused TP supports up to 8 ranks (one NVSwitch node)")
+        if S % self.world or (S // self.world) % 128:
+            raise ValueError("fused TP needs seq_len / tp to be a multiple of 128")
+        self.B, self.S, self.H = B, S, H
+        self.Sl = S // self.world
+        self.rows, self.rows_l = B * S, B * self.Sl
+        self.copy_saved = copy_saved
+        slot_bytes = self.rows * H * 2
+        self.off_fwd = self.SIG_BYTES
+        self.off_bwd = self.off_fwd + num_fwd_slots * slot_bytes
+        self.off_rs = self.off_bwd + 2 * slot_bytes
+        total = self.off_rs + self.world * self.rows_l * H * 2
+        self.num_fwd_slots = num_fwd_slots
+        self.slot_bytes = slot_bytes
+        self.symm = SymmetricBuffer(total, tp_group)
+        dev = self.symm.device
+        self.counters = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.ag_flag_ptrs = [self.symm.peer_ptr(r, 0) for r in range(self.world)]
+        self.rs_flag_ptrs = [self.symm.peer_ptr(r, 32) for r in range(self.world)]
+        self.ag_epoch = 0
+        self.rs_epoch = 0
+        self._bwd_next = 0
+        dist.barrier(group=tp_group)
+
+    # ---------------------------------------------------------------- buffers
+    def fwd_ptrs(self, i):
+        return [self.symm.peer_ptr(r, self.off_fwd + i * self.slot_bytes) for r in range(self.world)]
+
+    def fwd_view(self, i):
+        return self.symm.tensor(self.off_fwd + i * self.slot_bytes, self.rows * self.H, torch.bfloat16).view(
+            self.rows, self.H)
+
+    def next_bwd(self):
+        k = self._bwd_next
+        self._bwd_next ^= 1
+        return k
+
+    def bwd_ptrs(self, k):
+        return [self.symm.peer_ptr(r, self.off_bwd + k * self.slot_bytes) for r in range(self.world)]
+
+    def bwd_view(self, k):
+        return self.symm.tensor(self.off_bwd + k * self.slot_bytes, self.rows * self.H, torch.bfloat16).view(
+            self.rows, self.H)
+
+    def rs_dst_ptrs(self):
+        """For each owner rank: where THIS rank's partial rows go in the owner's slots."""
+        stride = self.rows_l * self.H * 2
+        return [self.symm.peer_ptr(r, self.off_rs + self.rank * stride) for r in range(self.world)]
+
+    @property
+    def rs_local_ptr(self):
+        return self.symm.peer_ptr(self.rank, self.off_rs)
+
+    # ---------------------------------------------------------------- fused ops
+    def ln_fwd_ag(self, x2, ln, slot):
+        """LayerNorm of the local shard; rows land in every rank's forward slot ``slot``."""
+        C = native()
+        self.ag_epoch += 1
+        mean = torch.empty(x2.shape[0], device=x2.device, dtype=torch.float32)
+        rstd = torch.empty_like(mean)
+        C.layernorm_fwd_push(x2, ln.weight.detach(), ln.bias.detach(), mean, rstd, ln.eps, self.fwd_ptrs(slot),
+                             self.ag_flag_ptrs, self.rank, self.ag_epoch, self.S, self.Sl, self.counters[0:1])
+        return self.fwd_view(slot), mean, rstd, self.ag_epoch
+
+    def ln_bwd_ag(self, dy_bf16, x2, mean, rstd, ln, dres, grad_target):
+        """LayerNorm backward of the local shard; bf16 dx rows land in every rank's next backward slot."""
+        C = native()
+        k = self.next_bwd()
+        self.ag_epoch += 1
+        dx = torch.empty_like(x2)
+        C.layernorm_bwd_push(dy_bf16, x2, mean, rstd, ln.weight.detach(), dres, dx, grad_target(ln.weight),
+                             grad_target(ln.bias), self.bwd_ptrs(k), self.ag_flag_ptrs, self.rank, self.ag_epoch,
+                             self.S, self.Sl, self.counters[1:2])
+        dx._mmb_gathered = (self.bwd_view(k), self.ag_epoch)
+        return dx
+
+    def gather_grad(self, d_local):
+        """Gathered bf16 copy of a local gradient shard: reuses the producer's push if there was one."""
+        g = getattr(d_local, "_mmb_gathered", None)
+        if g is not None:
+            return g
+        C = native()
+        k = self.next_bwd()
+        self.ag_epoch += 1
+        src = d_local.reshape(-1, self.H).to(torch.bfloat16).contiguous()
+        C.tp_ag_push(src, self.bwd_ptrs(k), self.ag_flag_ptrs, self.rank, self.ag_epoch, self.S, self.Sl,
+                     self.counters[2:3])
+        return self.bwd_view(k), self.ag_epoch
+
+    def gemm_ag(self, A_full, ag_epoch, W, w_mn, out, epi=0, aux=None):
+        """out = A_full (gathered, waited on per source rank) x W (Column forward / Row dgrad)."""
+        native().gemm_tp(A_full, False, W, w_mn, out, epi, aux, self.ag_flag_ptrs[self.rank], ag_epoch, self.S,
+                         self.Sl, [], [], self.rank, 0, None, out.shape[1])
+        return out
+
+    def gemm_rs(self, A, W, w_mn):
+        """Partial A x W pushed tile by tile to the owning ranks' reduce-scatter slots."""
+        C = native()
+        self.rs_epoch += 1
+        C.gemm_tp(A, False, W, w_mn, None, C.EPI_PUSH_BF16, None, 0, 0, self.S, self.Sl, self.rs_dst_ptrs(),
+                  self.rs_flag_ptrs, self.rank, self.rs_epoch, self.counters[3:4], self.H)
+        return self.rs_epoch
+
+    def rs_reduce(self, epoch, resid=None, out_bf16=False):
+        """Wait for every rank's partial rows of this shard; return resid + sum (fp32) or the sum in bf16."""
+        C = native()
+        n = self.rows_l * self.H
+        dev = self.symm.device
+        if out_bf16:
+            o16 = torch.empty(self.rows_l, self.H, device=dev, dtype=torch.bfloat16)
+            C.tp_rs_reduce(self.rs_local_ptr, n, self.world, self.rs_flag_ptrs[self.rank], epoch, resid, None, o16, n)
+            return o16
+        out = torch.empty(self.rows_l, self.H, device=dev, dtype=torch.float32)
+        C.tp_rs_reduce(self.rs_local_ptr, n, self.world, self.rs_flag_ptrs[self.rank], epoch, resid, out, None, n)
+        return out
+
+    def close(self):
+        if self.symm is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self.symm.close()
+            self.symm = None

@@ -76,6 +76,8 @@ class TrainConfig:
     num_steps: int = 100
     dp_overlap: bool = True
     dp_impl: str = "auto"               # "fused" (NVLink kernel), "nccl", or "auto" (fused on CUDA when dp > 1)
+    tp_impl: str = "auto"               # "fused" (collectives inside LN/GEMM kernels; implies sequence
+                                        # parallelism), "nccl", or "auto" (fused on CUDA when tp > 1)
     bucket_mb: float = 64.0
     recompute: bool = False
     average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
@@ -91,7 +93,13 @@ class Trainer:
         self.device = torch.device(device)
         if not dist.is_initialized():
             raise RuntimeError("torch.distributed must be initialised (world size 1 is fine)")
-        self.mpu = mpu or pg.init_model_parallel(cfg.tp, cfg.pp, cfg.sequence_parallel)
+        seq_len = cfg.seq_len or cfg.model.max_seq_len
+        fused_tp = (self.device.type == "cuda" and cfg.tp > 1 and cfg.tp_impl in ("auto", "fused")
+                    and seq_len % cfg.tp == 0 and (seq_len // cfg.tp) % 128 == 0)
+        if cfg.tp_impl == "fused" and not fused_tp and cfg.tp > 1:
+            raise ValueError("fused TP needs CUDA and seq_len / tp divisible by 128")
+        self.tp_impl = "fused" if fused_tp else "nccl"
+        self.mpu = mpu or pg.init_model_parallel(cfg.tp, cfg.pp, cfg.sequence_parallel or fused_tp)
         pg.set_model_parallel(self.mpu)
         mpu = self.mpu
         self.seq_len = cfg.seq_len or cfg.model.max_seq_len
@@ -134,6 +142,14 @@ class Trainer:
                                         weight_decay=cfg.weight_decay, grad_scale=grad_scale)
             self.grad_sync = GradSync(self.buf, mpu["dp_group"], mode="allreduce", overlap=cfg.dp_overlap)
         layers = self.model.decoder_layers if cfg.pp > 1 else self.model.decoder.layers
+        self.tp_ws = None
+        if self.tp_impl == "fused":
+            from .parallel.fused_tp import TPWorkspace
+            self.tp_ws = TPWorkspace(mpu["tp_group"], cfg.micro_batch_size, self.seq_len, cfg.model.hidden_size,
+                                     num_fwd_slots=2 * len(layers), copy_saved=cfg.pp > 1)
+            for i, layer in enumerate(layers):
+                layer._mmb_tp_ws = self.tp_ws
+                layer._mmb_tp_slot = i
         self.grad_sync.attach(list(layers))
         self.scheduler = torch.optim.lr_scheduler.LambdaLR(self.optimizer,
                                                            make_lr_lambda(cfg.warmup_steps, cfg.num_steps))
@@ -203,6 +219,9 @@ class Trainer:
         return self.model, self.optimizer, self.scheduler
 
     def destroy(self):
+        if self.tp_ws is not None:
+            self.tp_ws.close()
+            self.tp_ws = None
         if hasattr(self.optimizer, "close"):
             self.optimizer.close()
         pg.set_model_parallel(None)

@@ -51,12 +51,12 @@ def _run(fn, world, *args, port=29711):
         return [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
 
 
-def _train(rank, world, tp, pp, sp, dp_impl, steps, micro):
+def _train(rank, world, tp, pp, sp, dp_impl, steps, micro, tp_impl="auto"):
     from mini_megatron_b200.config import GPTConfig
     from mini_megatron_b200.training import TrainConfig, Trainer, synthetic_batch
     cfg = TrainConfig(model=GPTConfig(**CFG), micro_batch_size=2, seq_len=256, num_microbatches=micro, tp=tp, pp=pp,
-                      sequence_parallel=sp, dp_impl=dp_impl, lr=1e-3, warmup_steps=0, num_steps=100,
-                      bucket_mb=1.0)
+                      sequence_parallel=sp, dp_impl=dp_impl, tp_impl=tp_impl, lr=1e-3, warmup_steps=0,
+                      num_steps=100, bucket_mb=1.0)
     t = Trainer(cfg)
     dp_rank = t.mpu["dp_rank"]
     losses = []
@@ -103,3 +103,17 @@ def test_native_pp2_runs_and_loss_is_sane():
     last = res[1]["losses"]
     assert all(x is not None for x in last) and abs(last[0] - 6.9) < 0.3, last
     assert res[0]["losses"] == [None, None, None]
+
+
+@NEED2
+def test_fused_tp_matches_nccl_tp():
+    """Collectives fused into the LN / GEMM kernels reproduce the NCCL sequence-parallel path."""
+    fused = _run(_train, 2, 2, 1, True, "nccl", 3, 2, "fused", port=29717)
+    nccl = _run(_train, 2, 2, 1, True, "nccl", 3, 2, "nccl", port=29718)
+    for r in range(2):
+        for a, b in zip(fused[r]["losses"], nccl[r]["losses"]):
+            assert abs(a - b) < 2e-3 * abs(b), (fused[r]["losses"], nccl[r]["losses"])
+        for k, v in fused[r]["state"].items():
+            ref = nccl[r]["state"][k]
+            rel = ((v - ref).norm() / (ref.norm() + 1e-12)).item()
+            assert rel < 2e-3, (k, rel)
