@@ -1,6 +1,6 @@
 """Headline benchmark: GPT-125M training tokens/s on N B200s (DP=N, weak scaling).
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--config NAME]
 
 For N > 1 launch one process per GPU:
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
@@ -10,6 +10,14 @@ Config: GPT-125M (12 layers, hidden 768, 12 heads, FFN 3072,
 vocab 50257, learned positions, pre-LN, GELU, no bias), TP=1 PP=1 DP=N,
 micro-batch 16 per GPU, seq 1024, bf16 compute with fp32 AdamW, synthetic
 uniform-random tokens with next-token labels, random N(0, 0.02) init.
+
+``--config`` selects the other BASELINE configs (dp = N / (tp * pp)):
+gpt125m-tp2pp2 (125M, TP2 PP2, 8 microbatches of 8 x 1024, sequence parallel),
+gpt1.3b-tp8sp (1.3B, TP8 with sequence parallelism, micro-batch 4 x 2048) and
+gpt6.7b-tp4pp2 (6.7B, TP4 PP2, 16 microbatches of 2 x 2048, ZeRO-1 when dp > 1).
+The reference arm runs the same shapes through its own modules (no sequence
+parallelism: the reference does not wire it) and, for pp > 1, its own
+``train_pipeline_1f1b``.
 
 Timing: W untimed warm-up steps, then EXACTLY K steps bracketed by a barrier
 and torch.cuda.synchronize() on both sides, timed with CUDA events on the
@@ -47,6 +55,18 @@ METRIC = "GPT train tok/s (device-timed, max over ranks) at 1/2/4/8 B200 vs ref'
 MODEL = dict(num_layers=12, hidden_size=768, num_attention_heads=12, ffn_hidden_size=3072, max_seq_len=1024,
              vocab_size=50257)
 BASELINE_VALUE = None  # BASELINE.md publishes no B200 number for this config
+M_1_3B = dict(num_layers=24, hidden_size=2048, num_attention_heads=16, ffn_hidden_size=8192, max_seq_len=2048,
+              vocab_size=50257)
+M_6_7B = dict(num_layers=32, hidden_size=4096, num_attention_heads=32, ffn_hidden_size=16384, max_seq_len=2048,
+              vocab_size=50257)
+# The BASELINE configs.  tp/pp are per config; dp = N / (tp * pp); a step is one
+# optimizer step over m microbatches of mb x seq tokens per DP replica.
+CONFIGS = {
+    "gpt125m-dp": dict(name="GPT-125M", model=MODEL, tp=1, pp=1, mb=16, m=1, seq=1024, sp=False, zero1=False),
+    "gpt125m-tp2pp2": dict(name="GPT-125M", model=MODEL, tp=2, pp=2, mb=8, m=8, seq=1024, sp=True, zero1=False),
+    "gpt1.3b-tp8sp": dict(name="GPT-1.3B", model=M_1_3B, tp=8, pp=1, mb=4, m=1, seq=2048, sp=True, zero1=False),
+    "gpt6.7b-tp4pp2": dict(name="GPT-6.7B", model=M_6_7B, tp=4, pp=2, mb=2, m=16, seq=2048, sp=True, zero1=True),
+}
 
 
 def parse():
@@ -55,17 +75,38 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--micro-batch-size", type=int, default=16)
-    ap.add_argument("--seq-len", type=int, default=1024)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt125m-dp",
+                    help="BASELINE config: gpt125m-dp (headline), gpt125m-tp2pp2, gpt1.3b-tp8sp, gpt6.7b-tp4pp2")
+    ap.add_argument("--tp", type=int, default=None, help="override the config's TP size")
+    ap.add_argument("--pp", type=int, default=None, help="override the config's PP size")
+    ap.add_argument("--micro-batch-size", type=int, default=None)
+    ap.add_argument("--num-microbatches", type=int, default=None)
+    ap.add_argument("--seq-len", type=int, default=None)
+    ap.add_argument("--tp-impl", default="auto", choices=["auto", "fused", "nccl"])
+    ap.add_argument("--dp-impl", default="auto", choices=["auto", "fused", "nccl"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    c = CONFIGS[args.config]
+    args.tp = args.tp or c["tp"]
+    args.pp = args.pp or c["pp"]
+    args.micro_batch_size = args.micro_batch_size or c["mb"]
+    args.num_microbatches = args.num_microbatches or c["m"]
+    args.seq_len = args.seq_len or c["seq"]
+    args.model = dict(c["model"], max_seq_len=args.seq_len)
+    args.model_name = c["name"]
+    args.sp = c["sp"]
+    args.zero1 = c["zero1"]
+    if args.gpus % (args.tp * args.pp):
+        raise SystemExit(f"--gpus {args.gpus} is not a multiple of tp*pp = {args.tp * args.pp}")
+    args.dp = args.gpus // (args.tp * args.pp)
+    return args
 
 
-def synthetic_batch(B, S, vocab, seed, pin=True):
-    """Uniform-random int64 tokens [1, B, S] with next-token labels (host, pinned)."""
+def synthetic_batch(B, S, vocab, seed, pin=True, m=1):
+    """Uniform-random int64 tokens [m, B, S] with next-token labels (host, pinned)."""
     g = torch.Generator().manual_seed(seed)
-    toks = torch.randint(0, vocab, (1, B, S + 1), generator=g)
+    toks = torch.randint(0, vocab, (m, B, S + 1), generator=g)
     tokens, labels = toks[..., :-1].contiguous(), toks[..., 1:].contiguous()
     if pin:
         tokens, labels = tokens.pin_memory(), labels.pin_memory()
@@ -167,12 +208,16 @@ def build_ours(args, rank):
     sys.path.insert(0, HERE)
     from mini_megatron_b200.config import GPTConfig
     from mini_megatron_b200.training import TrainConfig, Trainer
-    cfg = TrainConfig(model=GPTConfig(**MODEL), micro_batch_size=args.micro_batch_size, seq_len=args.seq_len,
-                      num_microbatches=1, lr=6e-4, weight_decay=0.1, warmup_steps=10, num_steps=1000)
+    m = args.num_microbatches
+    cfg = TrainConfig(model=GPTConfig(**args.model), micro_batch_size=args.micro_batch_size, seq_len=args.seq_len,
+                      num_microbatches=m, tp=args.tp, pp=args.pp, sequence_parallel=args.sp and args.tp > 1,
+                      zero1=args.zero1 and args.dp > 1, lr=6e-4, weight_decay=0.1, warmup_steps=10, num_steps=1000,
+                      tp_impl=args.tp_impl, dp_impl=args.dp_impl)
     trainer = Trainer(cfg)
-    nb = 4
-    batches = [synthetic_batch(args.micro_batch_size, args.seq_len, MODEL["vocab_size"], seed=1000 * rank + i)
-               for i in range(nb)]
+    dp_rank = trainer.mpu["dp_rank"]
+    nb = 4 if m == 1 else 2
+    batches = [synthetic_batch(args.micro_batch_size, args.seq_len, args.model["vocab_size"],
+                               seed=1000 * dp_rank + i, m=m) for i in range(nb)]
 
     def step_host(i):
         tok, lab = batches[i % nb]
@@ -184,7 +229,9 @@ def build_ours(args, rank):
         tok, lab = dev[i % nb]
         return trainer.train_step(tok, lab)
 
-    return step_dev, step_host, sum(t.numel() for t, _ in batches[:1])
+    info = {"tp_impl": trainer.tp_impl, "dp_impl": trainer.dp_impl,
+            "sequence_parallel": bool(trainer.mpu["sequence_parallel"]), "zero1": bool(cfg.zero1)}
+    return step_dev, step_host, args.micro_batch_size * args.seq_len * m, info
 
 
 # ----------------------------------------------------------------------------- reference
@@ -193,55 +240,106 @@ def build_reference(args, rank):
     if not os.path.exists(os.path.join(ref, "main.py")):
         return None
     sys.path.insert(0, ref)
+    import contextlib
+    import io
+
     import config as rcfg  # the reference's config module
-    rcfg.NUM_LAYERS, rcfg.HIDDEN_SIZE = MODEL["num_layers"], MODEL["hidden_size"]
-    rcfg.NUM_ATTENTION_HEADS, rcfg.FFN_HIDDEN_SIZE = MODEL["num_attention_heads"], MODEL["ffn_hidden_size"]
-    rcfg.MAX_SEQ_LEN, rcfg.VOCAB_SIZE = args.seq_len, MODEL["vocab_size"]
+    tp, pp, m = args.tp, args.pp, args.num_microbatches
+    # The reference's VocabParallelEmbedding needs V % tp == 0 (tensor_parallel.py:91-92):
+    # at tp > 1 it runs its own default vocabulary, 50304 (config.py), the padded size we compute with too.
+    vocab = args.model["vocab_size"] if tp == 1 else 50304
+    rcfg.NUM_LAYERS, rcfg.HIDDEN_SIZE = args.model["num_layers"], args.model["hidden_size"]
+    rcfg.NUM_ATTENTION_HEADS, rcfg.FFN_HIDDEN_SIZE = args.model["num_attention_heads"], args.model["ffn_hidden_size"]
+    rcfg.MAX_SEQ_LEN, rcfg.VOCAB_SIZE = args.seq_len, vocab
     from main import make_lr_lambda
     from model.embedding import Embedding
     from model.loss import CrossEntropyLoss
-    from model.transformer import GPT, Decoder
+    from model.transformer import GPT, Decoder, DecoderLayer
     from parallel.data_parallel import allreduce_grads
+    from parallel.pipeline_parallel import train_pipeline_1f1b
     from parallel.process_groups import init_model_parallel, set_model_parallel
     from parallel.tensor_parallel import ColumnParallelLinear
     rcfg.enable_tf32()
-    mpu = init_model_parallel(1, 1)
+    mpu = init_model_parallel(tp, pp)
     set_model_parallel(mpu)
     torch.manual_seed(42)
     c = rcfg.get_model_config()
     dev = torch.device("cuda", torch.cuda.current_device())
     V, H, S = c["vocab_size"], c["hidden_size"], c["max_seq_len"]
-    model = GPT(Embedding(V, H, S).to(dev), Decoder(H, c["num_attention_heads"], c["ffn_hidden_size"],
-                                                   c["num_layers"]).to(dev),
-                torch.nn.LayerNorm(H).to(dev), ColumnParallelLinear(H, V, bias=False, gather_output=True).to(dev),
-                CrossEntropyLoss()).to(dev)
-    opt = torch.optim.AdamW(model.parameters(), lr=rcfg.LEARNING_RATE, weight_decay=rcfg.WEIGHT_DECAY, fused=True)
-    sched = torch.optim.lr_scheduler.LambdaLR(opt, make_lr_lambda(10, 1000))
+    NH, F, NL = c["num_attention_heads"], c["ffn_hidden_size"], c["num_layers"]
     amp = torch.autocast(device_type="cuda", dtype=torch.bfloat16)
     B = args.micro_batch_size
-    mask = torch.ones(B, S, dtype=torch.float32, device=dev)
-    nb = 4
-    batches = [synthetic_batch(B, S, V, seed=1000 * rank + i) for i in range(nb)]
-    devb = [(t[0].to(dev), l[0].to(dev)) for t, l in batches]
+    dp_rank = mpu["dp_rank"] if mpu else 0
+    nb = 4 if m == 1 else 2
+    batches = [synthetic_batch(B, S, V, seed=1000 * dp_rank + i, m=m) for i in range(nb)]
+    devb = [(t.to(dev), l.to(dev)) for t, l in batches]
+    info = {"tp_impl": "reference (NCCL all-reduce, no sequence parallelism)" if tp > 1 else None,
+            "dp_impl": "reference (per-parameter NCCL all-reduce)" if args.dp > 1 else None, "vocab": V}
 
-    def one(tok, lab):
-        opt.zero_grad()
-        with amp:
-            _, loss = model(tok, lab, mask)
-        loss.backward()
-        allreduce_grads(model, mpu.get("dp_group"))
-        opt.step()
-        sched.step()
-        return loss
+    if pp == 1:
+        mask = torch.ones(B, S, dtype=torch.float32, device=dev)
+        model = GPT(Embedding(V, H, S).to(dev), Decoder(H, NH, F, NL).to(dev), torch.nn.LayerNorm(H).to(dev),
+                    ColumnParallelLinear(H, V, bias=False, gather_output=True).to(dev), CrossEntropyLoss()).to(dev)
+        opt = torch.optim.AdamW(model.parameters(), lr=rcfg.LEARNING_RATE, weight_decay=rcfg.WEIGHT_DECAY,
+                                fused=True)
+        sched = torch.optim.lr_scheduler.LambdaLR(opt, make_lr_lambda(10, 1000))
+
+        def one(tok, lab):
+            opt.zero_grad()
+            loss = None
+            for mb in range(m):
+                with amp:
+                    _, loss = model(tok[mb], lab[mb], mask)
+                loss.backward()
+            allreduce_grads(model, mpu.get("dp_group"))
+            opt.step()
+            sched.step()
+            return loss
+    else:
+        # main.py's PP branch (main.py:116-160): stage modules + train_pipeline_1f1b, one optimizer step per call
+        pp_rank = mpu["pp_rank"]
+        per = NL // pp
+        start = pp_rank * per
+        end = start + per if pp_rank < pp - 1 else NL
+        embedding = Embedding(V, H, S).to(dev) if pp_rank == 0 else None
+        layers = torch.nn.ModuleList([DecoderLayer(H, NH, F).to(dev) for _ in range(start, end)])
+        last = pp_rank == pp - 1
+        ln_f = torch.nn.LayerNorm(H).to(dev) if last else None
+        lm_head = ColumnParallelLinear(H, V, bias=False, gather_output=True).to(dev) if last else None
+        loss_fn = CrossEntropyLoss().to(dev) if last else None
+        params = (list(embedding.parameters()) if embedding is not None else []) + list(layers.parameters())
+        params += (list(ln_f.parameters()) + list(lm_head.parameters())) if last else []
+        opt = torch.optim.AdamW(params, lr=rcfg.LEARNING_RATE, weight_decay=rcfg.WEIGHT_DECAY, fused=True)
+        sched = torch.optim.lr_scheduler.LambdaLR(opt, make_lr_lambda(10, 1000))
+        g_rank = dist.get_rank()
+
+        def one(tok, lab):
+            it = iter([(tok[mb], lab[mb]) for mb in range(m)])
+            with contextlib.redirect_stdout(io.StringIO()):   # its per-call report lines
+                train_pipeline_1f1b(embedding, layers, ln_f, lm_head, loss_fn, opt, sched, it, B, S, V, dev, m,
+                                    pp_rank, pp, g_rank, H, tp, 10 ** 9, mpu.get("dp_group"), amp)
+            return None
 
     def step_dev(i):
         return one(*devb[i % nb])
 
     def step_host(i):
         t, l = batches[i % nb]
-        return one(t[0].to(dev, non_blocking=True), l[0].to(dev, non_blocking=True))
+        return one(t.to(dev, non_blocking=True), l.to(dev, non_blocking=True))
 
-    return step_dev, step_host, B * S
+    return step_dev, step_host, B * S * m, info
+
+
+def parallelism_name(args):
+    parts = [f"tp{args.tp}"] if args.tp > 1 else []
+    parts += [f"pp{args.pp}"] if args.pp > 1 else []
+    parts += [f"dp{args.dp}"] if args.dp > 1 or not parts else []
+    name = "".join(parts)
+    if args.sp and args.tp > 1:
+        name += "-sp"
+    if args.zero1 and args.dp > 1:
+        name += "-zero1"
+    return name
 
 
 def count_launches(step_fn):
@@ -278,7 +376,7 @@ def main():
             return
     else:
         built = build_ours(args, rank)
-    step_dev, step_host, tokens_per_step_rank = built
+    step_dev, step_host, tokens_per_replica, info = built
     K, W = args.steps, args.warmup
     for i in range(W):
         step_dev(i)
@@ -288,7 +386,7 @@ def main():
     time.sleep(1.0)  # let nvidia-smi start sampling before the timed region
     ms = time_steps(step_dev, K)
     clocks = sampler.stop(list(range(N)))
-    tokens = tokens_per_step_rank * N * K
+    tokens = tokens_per_replica * args.dp * K
     value = tokens / (ms / 1e3)
     e2e = None
     if not args.no_e2e:
@@ -299,9 +397,10 @@ def main():
         t0 = time.perf_counter()
         e2e_ms = time_steps(e2e_step, K)
         wall = max_over_ranks(time.perf_counter() - t0)
-        B, S = args.micro_batch_size, args.seq_len
+        B, S, m = args.micro_batch_size, args.seq_len, args.num_microbatches
         e2e = {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(e2e_ms / K, 3),
-               "wall_s": round(wall, 3), "h2d_bytes_per_step": 2 * B * S * 8, "d2h_bytes_per_step": 4,
+               "wall_s": round(wall, 3), "h2d_bytes_per_step": 2 * m * B * S * 8,
+               "d2h_bytes_per_step": 4,
                "api": "mini_megatron_b200.training.Trainer.train_step" if args.impl == "ours" else
                "reference modules + main.py loop"}
     launches = None
@@ -320,9 +419,12 @@ def main():
             "ms_per_step": round(ms / K, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
             "dtype": "bf16", "data": "synthetic (uniform-random tokens, next-token labels; random N(0,0.02) init)",
-            "config": {"model": "GPT-125M", "global_batch": args.micro_batch_size * N, "seq_len": args.seq_len,
-                       "micro_batch_per_gpu": args.micro_batch_size, "vocab": MODEL["vocab_size"],
-                       "parallelism": f"dp{N}", "l2": "no flush: per-step working set (>1.6 GB logits) >> 126 MB L2"},
+            "config": {"model": args.model_name, "global_batch": args.micro_batch_size * args.num_microbatches * args.dp,
+                       "seq_len": args.seq_len, "micro_batch": args.micro_batch_size,
+                       "num_microbatches": args.num_microbatches, "vocab": args.model["vocab_size"],
+                       "parallelism": parallelism_name(args), "bench_config": args.config, **{k: v for k, v in
+                                                                                             info.items() if v is not None},
+                       "l2": "no flush: per-step working set (>= 1 GB of activations and logits) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e,
         }
         if args.impl == "ours":

@@ -1,5 +1,11 @@
 // Python bindings for the sm_100a kernels.  Only this translation unit
 // includes the torch headers; kernels live in plain .cu files.
+#include <execinfo.h>
+#include <signal.h>
+#include <sys/syscall.h>
+#include <unistd.h>
+
+#include <cstdio>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -512,11 +518,46 @@ void gemm_tp(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const c10::
   TORCH_CHECK(rc == 0, "gemm_tp launch failed, code ", rc);
 }
 
+// ----------------------------------------------------------------- crash diagnostics
+// Optional SIGSEGV/SIGBUS handler that prints the faulting address, the thread
+// id and a native backtrace to stderr, then hands over to the previous handler
+// (e.g. Python's faulthandler) so the process still dies with the signal.
+struct sigaction g_prev_segv, g_prev_bus;
+
+void crash_handler(int sig, siginfo_t* info, void* uctx) {
+  char buf[160];
+  const int n = snprintf(buf, sizeof buf, "mmb: signal %d at address %p in thread %ld; native backtrace:\n", sig,
+                         info ? info->si_addr : nullptr, (long)syscall(SYS_gettid));
+  if (n > 0) (void)!write(2, buf, (size_t)n);
+  void* frames[64];
+  const int k = backtrace(frames, 64);
+  backtrace_symbols_fd(frames, k, 2);
+  struct sigaction* prev = sig == SIGSEGV ? &g_prev_segv : &g_prev_bus;
+  if (prev->sa_flags & SA_SIGINFO) {
+    if (prev->sa_sigaction) prev->sa_sigaction(sig, info, uctx);
+  } else if (prev->sa_handler != SIG_DFL && prev->sa_handler != SIG_IGN && prev->sa_handler) {
+    prev->sa_handler(sig);
+  }
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+
+void install_crash_handler() {
+  struct sigaction sa {};
+  sa.sa_sigaction = crash_handler;
+  sa.sa_flags = SA_SIGINFO | SA_ONSTACK;
+  sigemptyset(&sa.sa_mask);
+  sigaction(SIGSEGV, &sa, &g_prev_segv);
+  sigaction(SIGBUS, &sa, &g_prev_bus);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of mini_megatron_b200";
   m.def("get_error", &get_error, "read the device error word (0 = ok)");
+  m.def("install_crash_handler", &install_crash_handler,
+        "print a native backtrace on SIGSEGV/SIGBUS before the previous handler runs");
   m.def("clear_error", &clear_error);
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("D"), py::arg("epi"), py::arg("aux") = c10::nullopt,

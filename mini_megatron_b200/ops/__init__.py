@@ -9,6 +9,7 @@ modules are the CPU oracle used by the unit tests.
 from __future__ import annotations
 
 import importlib
+import os
 
 _C = None
 _IMPORT_ERROR = None
@@ -20,6 +21,8 @@ def native():
     if _C is None:
         try:
             _C = importlib.import_module("mini_megatron_b200._C")
+            if os.environ.get("MMB_CRASH_TRACE") == "1":
+                _C.install_crash_handler()
         except ImportError as exc:  # pragma: no cover - exercised only without a build
             _IMPORT_ERROR = exc
             raise RuntimeError(
