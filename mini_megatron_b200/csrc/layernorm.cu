@@ -277,6 +277,11 @@ int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bf
 }
 
 // Number of fp32 [2H] partial rows the backward needs as scratch.
+// Static shared memory a row-pass kernel may add on top of its dynamic
+// partial-sum buffer (the completion word of the all-gather push variant);
+// above 48 KB in total the dynamic size must be opted in explicitly.
+constexpr int kLnStaticSmem = 256;
+
 int layernorm_bwd_parts(int rows, int H, int num_sms) {
   const int nv = (H / 4 + 31) / 32;
   if (nv <= 8) return std::min(4 * num_sms, std::max(1, (rows + 7) / 8));  // one per CTA of 8 warps
@@ -299,7 +304,7 @@ int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, c
     const int smem = 8 * 2 * (H / 4) * 16;
 #define LN_BWD(NVV)                                                                                      \
   do {                                                                                                   \
-    if (smem > 48 * 1024)                                                                                \
+    if (smem + kLnStaticSmem > 48 * 1024)                                                                \
       cudaFuncSetAttribute(ln_bwd_kernel<NVV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
     ln_bwd_kernel<NVV, true><<<blocks, 256, smem, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16, part, rows, H); \
   } while (0)
@@ -348,7 +353,7 @@ int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mea
     const int smem = 8 * 2 * (H / 4) * 16;
 #define LN_BWDP(NVV)                                                                                               \
   do {                                                                                                             \
-    if (smem > 48 * 1024)                                                                                          \
+    if (smem + kLnStaticSmem > 48 * 1024)                                                                          \
       cudaFuncSetAttribute(ln_bwd_kernel<NVV, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);     \
     ln_bwd_kernel<NVV, true, true><<<nparts, 256, smem, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, part, rows, \
                                                              H, push);                                              \

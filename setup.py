@@ -35,6 +35,12 @@ setup(
             sources=sources,
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            # Link the C++ runtime that torch itself uses (the shared system
+            # libstdc++).  A toolchain whose libstdc++.so link is missing would
+            # otherwise fall back to libstdc++.a, and a second, static copy of
+            # the C++ runtime inside the extension breaks iostream formatting
+            # (every error message built by TORCH_CHECK).
+            extra_link_args=["-l:libstdc++.so.6"],
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
