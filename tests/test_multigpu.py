@@ -20,13 +20,13 @@ CFG = dict(num_layers=2, hidden_size=256, num_attention_heads=4, ffn_hidden_size
            vocab_size=1000)
 
 
-def _entry(rank, world, port, fn, args, out):
+def _entry(rank, world, port, fn, args, out, env):
     import datetime
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", **env)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
@@ -37,10 +37,10 @@ def _entry(rank, world, port, fn, args, out):
         dist.destroy_process_group()
 
 
-def _run(fn, world, *args, port=29711):
+def _run(fn, world, *args, port=29711, env=None):
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
-        ps = [ctx.Process(target=_entry, args=(r, world, port, fn, args, d)) for r in range(world)]
+        ps = [ctx.Process(target=_entry, args=(r, world, port, fn, args, d, env or {})) for r in range(world)]
         for p in ps:
             p.start()
         for p in ps:
@@ -117,3 +117,21 @@ def test_fused_tp_matches_nccl_tp():
             ref = nccl[r]["state"][k]
             rel = ((v - ref).norm() / (ref.norm() + 1e-12)).item()
             assert rel < 2e-3, (k, rel)
+
+
+@NEED2
+def test_fused_tp_poisoned_workspace_gives_identical_results():
+    """Debug mode: every data region of the TP workspace is NaN-filled before each step.
+    A kernel that read a gathered row or reduce-scatter slot before its producer wrote it
+    in the same step would turn the loss into NaN; results must match the clean run instead
+    (up to the order of floating-point reductions, which split-K and atomics leave open)."""
+    clean = _run(_train, 2, 2, 1, True, "nccl", 2, 2, "fused", port=29719)
+    poisoned = _run(_train, 2, 2, 1, True, "nccl", 2, 2, "fused", port=29720, env={"MMB_POISON_SYMM": "1"})
+    for r in range(2):
+        assert poisoned[r]["losses"][0] == clean[r]["losses"][0]           # first forward: no reductions differ
+        for a, b in zip(poisoned[r]["losses"], clean[r]["losses"]):
+            assert abs(a - b) <= 1e-4 * abs(b), (poisoned[r]["losses"], clean[r]["losses"])
+        for k, v in poisoned[r]["state"].items():
+            ref = clean[r]["state"][k]
+            assert torch.isfinite(v).all(), k
+            assert ((v - ref).norm() / (ref.norm() + 1e-12)).item() < 1e-4, k
