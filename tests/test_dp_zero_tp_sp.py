@@ -60,7 +60,7 @@ def test_dp2_matches_single_process(zero1, overlap):
     states = run_ranks(_dp_worker, 2, zero1, overlap)
     for st in states:
         for k, v in st.items():
-            torch.testing.assert_close(v, ref[k], atol=2e-6, rtol=1e-5, msg=k)
+            _assert_adam_step_close(v, ref[k], k)
 
 
 def _tp_worker(rank, world, sp):
