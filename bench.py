@@ -230,7 +230,9 @@ def build_ours(args, rank):
         return trainer.train_step(tok, lab)
 
     info = {"tp_impl": trainer.tp_impl, "dp_impl": trainer.dp_impl,
-            "sequence_parallel": bool(trainer.mpu["sequence_parallel"]), "zero1": bool(cfg.zero1)}
+            "sequence_parallel": bool(trainer.mpu["sequence_parallel"]), "zero1": bool(cfg.zero1),
+            "cuda_graph": bool(trainer.graph_mode)}
+    step_dev.trainer = trainer
     return step_dev, step_host, args.micro_batch_size * args.seq_len * m, info
 
 
@@ -415,7 +417,12 @@ def main():
     launches = None
     if not args.no_launch_count:
         try:
-            ours, other, names = count_launches(step_dev)
+            tr = getattr(step_dev, "trainer", None)
+            if tr is not None:   # count the kernels of one step run eagerly (a replayed graph launches the same set)
+                with tr.eager():
+                    ours, other, names = count_launches(step_dev)
+            else:
+                ours, other, names = count_launches(step_dev)
             launches = {"ours_per_step": ours, "other_per_step": other}
             if rank == 0 and os.environ.get("BENCH_KERNEL_LIST"):
                 with open(os.environ["BENCH_KERNEL_LIST"], "w") as f:

@@ -22,7 +22,13 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
                                                     float* __restrict__ m, float* __restrict__ v,
                                                     __nv_bfloat16* __restrict__ pb, long n, float lr, float b1,
                                                     float b2, float eps, float wd, float step_size,
-                                                    float bc2_sqrt, float grad_scale) {
+                                                    float bc2_sqrt, float grad_scale,
+                                                    const float* __restrict__ hyper) {
+  if (hyper) {  // step-dependent scalars from device memory (CUDA-graph replays)
+    lr = hyper[0];
+    step_size = hyper[1];
+    bc2_sqrt = hyper[2];
+  }
   const long n4 = n >> 2;
   const float decay = 1.f - lr * wd;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
@@ -65,13 +71,36 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
   }
 }
 
+// Advances the device step counter and derives this step's scalars, so that a
+// captured optimizer step replays correctly: lr = lr_table[step - 1] (the
+// schedule's value for this step, clamped to the table's end), then
+// hyper = {lr, lr / (1 - b1^step), sqrt(1 - b2^step)}.
+__global__ void adamw_hyper_kernel(int* __restrict__ step, const float* __restrict__ lr_table, int n_table, double b1,
+                                   double b2, float* __restrict__ hyper) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  const int s = *step + 1;
+  *step = s;
+  const float lr = lr_table[min(s - 1, n_table - 1)];
+  hyper[0] = lr;
+  hyper[1] = (float)((double)lr / (1.0 - pow(b1, (double)s)));
+  hyper[2] = (float)sqrt(1.0 - pow(b2, (double)s));
+}
+
+int adamw_hyper_step(int* step, const float* lr_table, int n_table, double b1, double b2, float* hyper,
+                     cudaStream_t s) {
+  if (n_table < 1) return -1;
+  adamw_hyper_kernel<<<1, 32, 0, s>>>(step, lr_table, n_table, b1, b2, hyper);
+  return (int)cudaGetLastError();
+}
+
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long n) {
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     y[i] = __float2bfloat16(x[i]);
 }
 
 int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, long n, float lr, float b1, float b2,
-               float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s) {
+               float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s,
+               const float* hyper) {
   if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(m) |
        reinterpret_cast<uintptr_t>(v)) & 15)
     return -1;
@@ -79,7 +108,7 @@ int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, 
   const long n4 = (n + 3) / 4;
   const int blocks = (int)std::min<long>((n4 + 255) / 256, (long)num_sms * 8);
   adamw_kernel<<<std::max(blocks, 1), 256, 0, s>>>(p, g, m, v, pb, n, lr, b1, b2, eps, wd, step_size, bc2_sqrt,
-                                                   grad_scale);
+                                                   grad_scale, hyper);
   return (int)cudaGetLastError();
 }
 

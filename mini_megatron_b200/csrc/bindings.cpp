@@ -249,6 +249,39 @@ void adamw_flat(Tensor& p, const Tensor& g, Tensor& m, Tensor& v, const c10::opt
   MMB_CHECK_RC(rc, "adamw_flat");
 }
 
+// AdamW whose lr / bias corrections come from `hyper` (device float[3]) -- the
+// form a CUDA graph can replay; `adamw_hyper_step` advances the device step.
+void adamw_flat_dev(Tensor& p, const Tensor& g, Tensor& m, Tensor& v, const c10::optional<Tensor>& pb,
+                    const Tensor& hyper, double b1, double b2, double eps, double wd, double grad_scale) {
+  check_f32(p, "p");
+  check_f32(g, "g");
+  check_f32(m, "m");
+  check_f32(v, "v");
+  check_f32(hyper, "hyper");
+  TORCH_CHECK(hyper.numel() >= 3, "hyper needs 3 floats");
+  TORCH_CHECK(p.numel() == g.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "adamw size mismatch");
+  __nv_bfloat16* pbp = nullptr;
+  if (pb.has_value()) {
+    check_bf16(*pb, "pb");
+    TORCH_CHECK(pb->numel() == p.numel(), "adamw bf16 shadow size mismatch");
+    pbp = reinterpret_cast<__nv_bfloat16*>(pb->data_ptr());
+  }
+  const int rc = mmb::adamw_flat(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                                 pbp, p.numel(), 0.f, (float)b1, (float)b2, (float)eps, (float)wd, 0.f, 1.f,
+                                 (float)grad_scale, num_sms(), cur_stream(), hyper.data_ptr<float>());
+  MMB_CHECK_RC(rc, "adamw_flat_dev");
+}
+
+void adamw_hyper_step(Tensor& step, const Tensor& lr_table, double b1, double b2, Tensor& hyper) {
+  check_cuda(step, "step");
+  TORCH_CHECK(step.scalar_type() == at::kInt && step.numel() == 1, "step must be one int32");
+  check_f32(lr_table, "lr_table");
+  check_f32(hyper, "hyper");
+  MMB_CHECK_RC(mmb::adamw_hyper_step(step.data_ptr<int>(), lr_table.data_ptr<float>(), (int)lr_table.numel(), b1, b2,
+                                     hyper.data_ptr<float>(), cur_stream()),
+               "adamw_hyper_step");
+}
+
 std::vector<Tensor> gelu_fwd_bwd_f32(const Tensor& x) {
   check_f32(x, "x");
   Tensor y = at::empty_like(x), g = at::empty_like(x);
@@ -444,13 +477,14 @@ void tp_ag_push(const Tensor& src, const std::vector<int64_t>& dst, const std::v
 // out = resid + sum of `world` bf16 slots [rows_l, H] (slot s at slots_ptr + s*slot_stride elements)
 void tp_rs_reduce(int64_t slots_ptr, int64_t slot_stride, int64_t world, int64_t flags_ptr, int64_t epoch,
                   const c10::optional<Tensor>& resid, const c10::optional<Tensor>& out,
-                  const c10::optional<Tensor>& out_bf16, int64_t n) {
+                  const c10::optional<Tensor>& out_bf16, int64_t n, int64_t timeout_ms) {
+  TORCH_CHECK(timeout_ms > 0, "tp_rs_reduce: timeout_ms must be positive");
   const float* r = resid.has_value() ? resid->data_ptr<float>() : nullptr;
   float* o = out.has_value() ? out->data_ptr<float>() : nullptr;
   __nv_bfloat16* ob = out_bf16.has_value() ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
   MMB_CHECK_RC(mmb::tp_rs_reduce(reinterpret_cast<const __nv_bfloat16*>(slots_ptr), slot_stride, (int)world,
                                  reinterpret_cast<const int*>(flags_ptr), (int)epoch, r, o, ob, n, error_word(),
-                                 num_sms(), cur_stream()),
+                                 num_sms(), cur_stream(), (unsigned long long)timeout_ms * 1000000ull),
                "tp_rs_reduce");
 }
 
@@ -571,6 +605,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("adamw_flat", &adamw_flat);
+  m.def("adamw_flat_dev", &adamw_flat_dev);
+  m.def("adamw_hyper_step", &adamw_hyper_step);
   m.def("cast_f32_bf16", &cast_f32_bf16);
   m.def("gelu_fwd_bwd_f32", &gelu_fwd_bwd_f32);
   m.def("symm_alloc", &symm_alloc);
@@ -584,7 +620,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_fwd_push", &layernorm_fwd_push);
   m.def("layernorm_bwd_push", &layernorm_bwd_push);
   m.def("tp_ag_push", &tp_ag_push);
-  m.def("tp_rs_reduce", &tp_rs_reduce);
+  m.def("tp_rs_reduce", &tp_rs_reduce, py::arg("slots_ptr"), py::arg("slot_stride"), py::arg("world"),
+        py::arg("flags_ptr"), py::arg("epoch"), py::arg("resid"), py::arg("out"), py::arg("out_bf16"), py::arg("n"),
+        py::arg("timeout_ms") = 10000);
   m.def("gemm_tp", &gemm_tp);
   m.attr("EPI_PUSH_BF16") = (int)mmb::EPI_PUSH_BF16;
   m.def("num_sms", &num_sms);

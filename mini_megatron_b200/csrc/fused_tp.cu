@@ -34,8 +34,9 @@ namespace mmb {
 __global__ void __launch_bounds__(256) tp_rs_reduce_kernel(const __nv_bfloat16* __restrict__ slots, long slot_stride,
                                                            int world, const int* __restrict__ flags, int epoch,
                                                            const float* __restrict__ resid, float* __restrict__ out,
-                                                           __nv_bfloat16* __restrict__ out_bf16, long n, int* err) {
-  if (!cta_wait_flags(flags, world, epoch, err)) return;
+                                                           __nv_bfloat16* __restrict__ out_bf16, long n, int* err,
+                                                           unsigned long long timeout_ns) {
+  if (!cta_wait_flags(flags, world, epoch, err, timeout_ns)) return;
   const long n8 = n >> 3;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
     float acc[8];
@@ -85,10 +86,11 @@ __global__ void __launch_bounds__(256) tp_ag_push_kernel(const __nv_bfloat16* __
 
 int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
                  const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
-                 cudaStream_t s) {
+                 cudaStream_t s, unsigned long long timeout_ns) {
   if (n % 8 != 0 || world < 1 || world > 8 || slot_stride % 8 != 0) return -1;
   const int blocks = (int)std::max<long>(1, std::min<long>((n / 8 + 255) / 256, (long)num_sms * 4));
-  tp_rs_reduce_kernel<<<blocks, 256, 0, s>>>(slots, slot_stride, world, flags, epoch, resid, out, out_bf16, n, err);
+  tp_rs_reduce_kernel<<<blocks, 256, 0, s>>>(slots, slot_stride, world, flags, epoch, resid, out, out_bf16, n, err,
+                                             timeout_ns);
   return (int)cudaGetLastError();
 }
 

@@ -84,6 +84,28 @@ __device__ __forceinline__ void stage_load(uint8_t* stg, const uint8_t* gbase, l
   }
 }
 
+// Register prefetch of the same 32-row x 128-byte window (the side input of the
+// residual / GELU-backward epilogues): lane l holds rows it*4 + l/8, unit l%8.
+// Issued one chunk ahead, so the global-load latency hides behind the current
+// chunk's TMEM load, math and store.
+__device__ __forceinline__ void side_prefetch(uint4 (&buf)[8], const uint8_t* gbase, long ld_bytes, int rows_valid,
+                                              int col_bytes_valid, int lane) {
+  const int unit = lane & 7;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int row = it * 4 + (lane >> 3);
+    buf[it] = (row < rows_valid && unit * 16 < col_bytes_valid)
+                  ? *reinterpret_cast<const uint4*>(gbase + (size_t)row * ld_bytes + unit * 16)
+                  : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+__device__ __forceinline__ void side_to_stage(uint8_t* stg, const uint4 (&buf)[8], int lane) {
+  const int unit = lane & 7;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) *reinterpret_cast<uint4*>(stage_unit(stg, it * 4 + (lane >> 3), unit)) = buf[it];
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -271,6 +293,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;   // which alternate chunks this warp takes
     uint8_t* stg = sStage + (warp - 2) * kStageBytes;
+    // side input (residual fp32 / gelu' bf16) of chunk ch of tile t, prefetched one chunk ahead
+    constexpr bool SIDE = (EPI == EPI_RESID || EPI == EPI_DGELU);
+    constexpr int SIDE_ES = (EPI == EPI_RESID) ? 4 : 2;
+    const uint8_t* side_base = SIDE ? reinterpret_cast<const uint8_t*>(EPI == EPI_RESID ? (const void*)args.resid
+                                                                                        : (const void*)args.aux)
+                                    : nullptr;
+    const long side_ld = (EPI == EPI_RESID) ? args.ld_resid : args.ld_aux;
+    uint4 side[8];
+    auto prefetch_side = [&](int tt, int ch) {
+      int pm, pn;
+      tile_coords(tt / splits, mtiles, ntiles, pm, pn);
+      const int pr0 = pm * BM + q * 32, pc0 = pn * BN + ch * W;
+      side_prefetch(side, side_base + ((size_t)pr0 * side_ld + pc0) * SIDE_ES, side_ld * SIDE_ES,
+                    min(32, args.M - pr0), (args.N - pc0) * SIDE_ES, lane);
+    };
+    // the chunk this warp handles after (t, ch): the next alternate chunk of this
+    // tile, else its first chunk of the next tile of this CTA (if any)
+    auto prefetch_next_side = [&](int tt, int ch) {
+      int nt = tt, nch = ch + 2, cm, cn;
+      tile_coords(tt / splits, mtiles, ntiles, cm, cn);
+      if (nch >= BN / W || cn * BN + nch * W >= args.N) {
+        nt = tt + gridDim.x;
+        nch = half;
+      }
+      if (nt < num_tiles) prefetch_side(nt, nch);
+    };
+    if constexpr (SIDE) {
+      if (blockIdx.x < num_tiles) prefetch_side(blockIdx.x, half);
+    }
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -292,7 +343,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
       for (int ch = half; ch < nchunks; ch += 2) {
         const int col0 = n0 + ch * W;
-        if (col0 >= args.N) break;  // warp-uniform
+        if (col0 >= args.N) {  // warp-uniform
+          if constexpr (SIDE) prefetch_next_side(t, ch);
+          break;
+        }
         float v[W];
         {
           uint32_t r[32];
@@ -312,7 +366,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
           }
         }
-        if (rows_valid <= 0) continue;
+        if (rows_valid <= 0) {
+          if constexpr (SIDE) prefetch_next_side(t, ch);
+          continue;
+        }
         const int colb_valid = (args.N - col0) * (OUT_BF16 ? 2 : 4);
         // the previous store from this warp's stage must have finished reading it
         if (lane == 0) bulk_wait_read<0>();
@@ -349,9 +406,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
                 make_uint4(act[4 * u], act[4 * u + 1], act[4 * u + 2], act[4 * u + 3]);
         } else if constexpr (EPI == EPI_DGELU) {
-          // stage <- gelu'(pre) tile (coalesced), then out = acc * gelu' in place
-          const uint8_t* src = reinterpret_cast<const uint8_t*>(args.aux) + ((size_t)r0 * args.ld_aux + col0) * 2;
-          stage_load(stg, src, args.ld_aux * 2, rows_valid, colb_valid, lane);
+          // stage <- prefetched gelu'(pre) chunk, prefetch the next one, then out = acc * gelu' in place
+          side_to_stage(stg, side, lane);
+          prefetch_next_side(t, ch);
           __syncwarp();
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
@@ -367,9 +424,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             *pu = make_uint4(o[0], o[1], o[2], o[3]);
           }
         } else if constexpr (EPI == EPI_RESID) {
-          // stage <- residual tile (coalesced), then out = resid + acc in place
-          const uint8_t* src = reinterpret_cast<const uint8_t*>(args.resid) + ((size_t)r0 * args.ld_resid + col0) * 4;
-          stage_load(stg, src, args.ld_resid * 4, rows_valid, colb_valid, lane);
+          // stage <- prefetched residual chunk, prefetch the next one, then out = resid + acc in place
+          side_to_stage(stg, side, lane);
+          prefetch_next_side(t, ch);
           __syncwarp();
 #pragma unroll
           for (int u = 0; u < 8; ++u) {

@@ -126,62 +126,91 @@ __global__ void __launch_bounds__(256) ln_fwd_push_kernel(const float* __restric
   grid_done_signal(P.flags, P.world, P.rank, P.epoch, P.counter);
 }
 
-// Row pass.  With FUSE_PARAM, each warp also accumulates dgamma/dbeta over the
-// rows it visits and writes them to part[global_warp][0:2H].
+// Row pass.  Every load of a row (x, dy and the residual gradient) is issued
+// before the two row reductions, so a warp keeps all of its row's bytes in
+// flight at once.  With FUSE_PARAM, each warp also accumulates dgamma/dbeta of
+// the rows it visits in its own slice of shared memory (each lane owns its
+// columns, so no atomics), and the CTA folds its 8 warps into one partial row
+// part[blockIdx.x][0:2H]; keeping these sums out of registers leaves room for
+// more resident warps.
 template <int NV, bool FUSE_PARAM, bool PUSH = false>
-__global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
+__global__ void __launch_bounds__(256, NV <= 6 ? 3 : 1) ln_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const float* __restrict__ x,
                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
                                                      const float* __restrict__ gamma, const float* __restrict__ dres,
                                                      float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
                                                      float* __restrict__ part, int rows, int H, const AgPush P = AgPush{}) {
   const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   const int nvec = H >> 2;
   const float4* g4 = reinterpret_cast<const float4*>(gamma);
-  float4 dg[FUSE_PARAM ? NV : 1], db[FUSE_PARAM ? NV : 1];
+  extern __shared__ float4 red[];  // FUSE_PARAM: [8 warps][2 * nvec] = (dgamma | dbeta) partial sums
+  float4* my_dg = red + wid * 2 * nvec;
+  float4* my_db = my_dg + nvec;
   if constexpr (FUSE_PARAM) {
 #pragma unroll
-    for (int i = 0; i < NV; ++i) dg[i] = db[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) my_dg[c] = my_db[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   for (int r = gw; r < rows; r += nwarps) {
-    const float mu = mean[r], rs = rstd[r];
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)r * H);
     const uint2* dyr = reinterpret_cast<const uint2*>(dy + (size_t)r * H);
-    float4 xh[NV], gdy[NV];
+    const float4* drr = dres ? reinterpret_cast<const float4*>(dres + (size_t)r * H) : nullptr;
+    // rows of up to 1024 columns also prefetch the residual gradient; wider rows
+    // load it after the reductions to stay within the register file
+    constexpr bool kPrefetchRes = NV <= 8;
+    float4 xv[NV], dv[kPrefetchRes ? NV : 1];
+    uint2 du[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        xv[i] = xr[c];
+        du[i] = dyr[c];
+        if constexpr (kPrefetchRes) dv[i] = drr ? drr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    const float mu = mean[r], rs = rstd[r];
     float a = 0.f, b = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
-        const float4 xv = xr[c];
         const float4 g = g4[c];
-        const uint2 du = dyr[c];
-        const float2 d01 = unpack_bf16x2(du.x), d23 = unpack_bf16x2(du.y);
-        xh[i] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
-        gdy[i] = make_float4(d01.x * g.x, d01.y * g.y, d23.x * g.z, d23.y * g.w);
-        a += gdy[i].x + gdy[i].y + gdy[i].z + gdy[i].w;
-        b += gdy[i].x * xh[i].x + gdy[i].y * xh[i].y + gdy[i].z * xh[i].z + gdy[i].w * xh[i].w;
+        const float2 d01 = unpack_bf16x2(du[i].x), d23 = unpack_bf16x2(du[i].y);
+        xv[i] = make_float4((xv[i].x - mu) * rs, (xv[i].y - mu) * rs, (xv[i].z - mu) * rs, (xv[i].w - mu) * rs);
+        const float4 gd = make_float4(d01.x * g.x, d01.y * g.y, d23.x * g.z, d23.y * g.w);
+        a += gd.x + gd.y + gd.z + gd.w;
+        b += gd.x * xv[i].x + gd.y * xv[i].y + gd.z * xv[i].z + gd.w * xv[i].w;
         if constexpr (FUSE_PARAM) {
-          dg[i].x += d01.x * xh[i].x; dg[i].y += d01.y * xh[i].y; dg[i].z += d23.x * xh[i].z; dg[i].w += d23.y * xh[i].w;
-          db[i].x += d01.x; db[i].y += d01.y; db[i].z += d23.x; db[i].w += d23.y;
+          float4 t = my_dg[c];
+          t.x += d01.x * xv[i].x; t.y += d01.y * xv[i].y; t.z += d23.x * xv[i].z; t.w += d23.y * xv[i].w;
+          my_dg[c] = t;
+          float4 u = my_db[c];
+          u.x += d01.x; u.y += d01.y; u.z += d23.x; u.w += d23.y;
+          my_db[c] = u;
         }
       }
     }
     a = warp_sum(a) / H;
     b = warp_sum(b) / H;
     float4* dxr = reinterpret_cast<float4*>(dx + (size_t)r * H);
-    const float4* drr = dres ? reinterpret_cast<const float4*>(dres + (size_t)r * H) : nullptr;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = lane + 32 * i;
       if (c < nvec) {
-        float4 o = make_float4(rs * (gdy[i].x - a - xh[i].x * b), rs * (gdy[i].y - a - xh[i].y * b),
-                               rs * (gdy[i].z - a - xh[i].z * b), rs * (gdy[i].w - a - xh[i].w * b));
-        if (drr) {
-          const float4 d = drr[c];
-          o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
-        }
+        const float4 g = g4[c];
+        const float2 d01 = unpack_bf16x2(du[i].x), d23 = unpack_bf16x2(du[i].y);
+        float4 res;
+        if constexpr (kPrefetchRes) res = dv[i];
+        else res = drr ? drr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 o = make_float4(rs * (d01.x * g.x - a - xv[i].x * b) + res.x,
+                               rs * (d01.y * g.y - a - xv[i].y * b) + res.y,
+                               rs * (d23.x * g.z - a - xv[i].z * b) + res.z,
+                               rs * (d23.y * g.w - a - xv[i].w * b) + res.w);
         dxr[c] = o;
         if (dx_bf16 || PUSH) {
           uint2 ob;
@@ -199,17 +228,7 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const __nv_bfloat16* __rest
     }
   }
   if constexpr (FUSE_PARAM) {
-    // reduce the 8 warps' partial sums in shared memory: one partial row per CTA
-    extern __shared__ float4 red[];  // [8 warps][2 * nvec]
-    const int wid = threadIdx.x >> 5;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int c = lane + 32 * i;
-      if (c < nvec) {
-        red[wid * 2 * nvec + c] = dg[i];
-        red[wid * 2 * nvec + nvec + c] = db[i];
-      }
-    }
+    // fold the 8 warps' partial sums: one partial row per CTA
     __syncthreads();
     float4* pg = reinterpret_cast<float4*>(part + (size_t)blockIdx.x * 2 * H);
     for (int c = threadIdx.x; c < 2 * nvec; c += blockDim.x) {

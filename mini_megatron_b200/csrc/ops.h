@@ -43,7 +43,8 @@ int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mea
 
 int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
                  const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
-                 cudaStream_t s);
+                 cudaStream_t s,
+                 unsigned long long timeout_ns = 10000000000ull);
 int tp_ag_push(const __nv_bfloat16* src, int rows, int H, const AgPush& push, int num_sms, cudaStream_t s);
 
 int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
@@ -57,7 +58,10 @@ int embedding_bwd(const long* ids, const float* dout, float* dwte, float* dwpe, 
                   long vend, cudaStream_t s);
 
 int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, long n, float lr, float b1, float b2,
-               float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s);
+               float eps, float wd, float step_size, float bc2_sqrt, float grad_scale, int num_sms, cudaStream_t s,
+               const float* hyper = nullptr);
+int adamw_hyper_step(int* step, const float* lr_table, int n_table, double b1, double b2, float* hyper,
+                     cudaStream_t s);
 int gelu_fwd_bwd_f32(const float* x, float* y, float* g, long n, int num_sms, cudaStream_t s);
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStream_t s);
 

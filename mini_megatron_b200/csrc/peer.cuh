@@ -22,11 +22,12 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 }
 
 // Bounded wait until *flag >= epoch (single thread).
-__device__ __forceinline__ bool wait_flag_ge(const int* flag, int epoch, int* err) {
+__device__ __forceinline__ bool wait_flag_ge(const int* flag, int epoch, int* err,
+                                             unsigned long long timeout_ns = kPeerTimeoutNs) {
   if (ld_acquire_sys(flag) >= epoch) return true;
   const unsigned long long t0 = globaltimer();
   while (ld_acquire_sys(flag) < epoch) {
-    if (globaltimer() - t0 > kPeerTimeoutNs) {
+    if (globaltimer() - t0 > timeout_ns) {
       if (err) atomicExch(err, kErrPeerWait);
       return false;
     }
@@ -35,9 +36,10 @@ __device__ __forceinline__ bool wait_flag_ge(const int* flag, int epoch, int* er
 }
 
 // CTA-wide: threads 0..n-1 each wait for flags[i] >= epoch; returns true if all arrived.
-__device__ __forceinline__ bool cta_wait_flags(const int* flags, int n, int epoch, int* err) {
+__device__ __forceinline__ bool cta_wait_flags(const int* flags, int n, int epoch, int* err,
+                                               unsigned long long timeout_ns = kPeerTimeoutNs) {
   bool ok = true;
-  if (threadIdx.x < n) ok = wait_flag_ge(flags + threadIdx.x, epoch, err);
+  if (threadIdx.x < n) ok = wait_flag_ge(flags + threadIdx.x, epoch, err, timeout_ns);
   return __syncthreads_and(ok) != 0;
 }
 

@@ -44,6 +44,22 @@ class FusedAdamW(torch.optim.Optimizer):
                 n = p.numel()
                 self.state[p] = {"exp_avg": m[o:o + n].view_as(p), "exp_avg_sq": v[o:o + n].view_as(p)}
 
+    def enable_device_schedule(self, lr_table: torch.Tensor):
+        """Read lr and the step count from device memory, so a captured step replays correctly.
+
+        ``lr_table[i]`` is the learning rate of optimizer step ``i + 1`` (the
+        LR schedule evaluated ahead of time); a device int32 step counter,
+        advanced by a one-thread kernel inside the step, indexes it and the
+        bias corrections are derived from it on the device.  Only the flat
+        CUDA buffers are supported (no loose parameters).
+        """
+        if self._loose:
+            raise ValueError("device-side schedule needs every parameter in a flat CUDA buffer")
+        dev = self._buffers[0][0].data.device
+        self._dev_step = torch.tensor([self._step], dtype=torch.int32, device=dev)
+        self._dev_hyper = torch.zeros(4, dtype=torch.float32, device=dev)
+        self._lr_table = lr_table.to(device=dev, dtype=torch.float32).contiguous()
+
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None
@@ -53,8 +69,15 @@ class FusedAdamW(torch.optim.Optimizer):
         if self._buffers:
             from .ops import native
             C = native()
-            for buf, m, v in self._buffers:
-                C.adamw_flat(buf.data, buf.grad, m, v, buf.bf16, lr, b1, b2, eps, wd, self._step, self.grad_scale)
+            if getattr(self, "_lr_table", None) is not None:
+                C.adamw_hyper_step(self._dev_step, self._lr_table, b1, b2, self._dev_hyper)
+                for buf, m, v in self._buffers:
+                    C.adamw_flat_dev(buf.data, buf.grad, m, v, buf.bf16, self._dev_hyper, b1, b2, eps, wd,
+                                     self.grad_scale)
+            else:
+                for buf, m, v in self._buffers:
+                    C.adamw_flat(buf.data, buf.grad, m, v, buf.bf16, lr, b1, b2, eps, wd, self._step,
+                                 self.grad_scale)
         bc1 = 1 - b1 ** self._step
         bc2_sqrt = math.sqrt(1 - b2 ** self._step)
         for group in self.param_groups:
@@ -108,6 +131,8 @@ class FusedAdamW(torch.optim.Optimizer):
                         views[p][k].copy_(st[k])
                         st[k] = views[p][k]
         self._step = max(steps) if steps else 0
+        if getattr(self, "_dev_step", None) is not None:
+            self._dev_step.fill_(self._step)
         for buf, _, _ in self._buffers:
             buf.refresh_bf16()
 

@@ -100,6 +100,8 @@ class TrainConfig:
     average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
     seed: int = 42
     nvtx: bool = False                  # NVTX ranges per phase (also MMB_NVTX=1)
+    cuda_graph: str = "auto"            # "on", "off", or "auto": replay each whole step as one CUDA graph
+                                        # where supported (CUDA, tp = pp = dp = 1, flat fused AdamW)
 
 
 class Trainer:
@@ -182,6 +184,7 @@ class Trainer:
         self.step_count = 0
         self.nvtx = cfg.nvtx or os.environ.get("MMB_NVTX") == "1"
         self.poison_symm = os.environ.get("MMB_POISON_SYMM") == "1"
+        self._setup_cuda_graph()
         # a collective on the default group before the first (batched) p2p
         if dist.get_world_size() > 1:
             t = torch.zeros(1, device=self.device)
@@ -196,7 +199,90 @@ class Trainer:
         if self.tp_ws is not None and self.poison_symm:
             self.tp_ws.poison()
         with _nvtx(self.nvtx, "train_step"):
+            if self.graph_mode:
+                return self._graph_step(tokens, labels, loss_mask)
             return self._train_step(tokens, labels, loss_mask)
+
+    # ------------------------------------------------------------------ CUDA graphs
+    GRAPH_WARMUP = 1
+
+    def _setup_cuda_graph(self):
+        """Decide whether whole steps are replayed from one captured CUDA graph.
+
+        A captured step launches its ~300 kernels with one call and no host
+        gaps between them.  Everything step-dependent must then live on the
+        device: the optimizer reads lr and its step count from device memory
+        (``FusedAdamW.enable_device_schedule``, lr precomputed from the
+        schedule), and the batch is copied into static input buffers before
+        each replay.  Supported for single-GPU chunks (tp = pp = dp = 1) with
+        the flat fused AdamW; other layouts run eagerly.
+        """
+        cfg = self.cfg
+        supported = (self.device.type == "cuda" and cfg.tp == 1 and cfg.pp == 1 and self.mpu["dp_size"] == 1
+                     and isinstance(self.optimizer, FusedAdamW) and not self.optimizer._loose)
+        if cfg.cuda_graph == "on" and not supported:
+            raise ValueError("cuda_graph='on' needs CUDA, tp = pp = dp = 1 and the flat fused AdamW")
+        self.graph_mode = supported and cfg.cuda_graph in ("on", "auto") and os.environ.get("MMB_CUDA_GRAPH") != "0"
+        self._graph = None
+        self._graph_calls = 0
+        if self.graph_mode:
+            lam = self.scheduler.lr_lambdas[0]
+            base = self.scheduler.base_lrs[0]
+            n = 2 * cfg.num_steps + 1024
+            table = torch.tensor([base * lam(i) for i in range(n)], dtype=torch.float32)
+            self.optimizer.enable_device_schedule(table)
+
+    def eager(self):
+        """Context manager: run the enclosed steps eagerly even in graph mode (e.g. under a profiler)."""
+        trainer = self
+
+        class _Eager:
+            def __enter__(self):
+                self.prev = trainer.graph_mode
+                trainer.graph_mode = False
+
+            def __exit__(self, *exc):
+                trainer.graph_mode = self.prev
+                return False
+        return _Eager()
+
+    def _graph_step(self, tokens, labels, loss_mask):
+        if tokens.dim() == 2:
+            tokens, labels = tokens.unsqueeze(0), labels.unsqueeze(0)
+        if self._graph is None and self._graph_calls < self.GRAPH_WARMUP:
+            # eager warm-up on a side stream (allocator and lazy initialisation settle before capture)
+            self._graph_calls += 1
+            side = torch.cuda.Stream(device=self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                out = self._train_step(tokens, labels, loss_mask)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            return out
+        first = self._graph is None
+        if first:
+            self._static_tokens = torch.empty(tokens.shape, dtype=tokens.dtype, device=self.device)
+            self._static_labels = torch.empty(labels.shape, dtype=labels.dtype, device=self.device)
+            self._static_mask = (self._loss_mask() if loss_mask is None else
+                                 torch.empty(loss_mask.shape, dtype=torch.float32, device=self.device))
+        if tokens.shape != self._static_tokens.shape:
+            raise ValueError("a captured step needs the same batch shape every step")
+        self._static_tokens.copy_(tokens, non_blocking=True)
+        self._static_labels.copy_(labels, non_blocking=True)
+        if loss_mask is not None:
+            self._static_mask.copy_(loss_mask, non_blocking=True)
+        if first:
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                self._static_loss = self._train_step(self._static_tokens, self._static_labels, self._static_mask)
+            self._graph = g
+            # capturing ran this step's host-side bookkeeping (scheduler, step counters) once; now run its kernels
+        else:
+            self.optimizer._step += 1
+            self.scheduler.step()
+            self.step_count += 1
+        self._graph.replay()
+        return None if self._static_loss is None else self._static_loss.clone()
 
     def _train_step(self, tokens, labels, loss_mask):
         cfg = self.cfg
@@ -249,6 +335,7 @@ class Trainer:
         return self.model, self.optimizer, self.scheduler
 
     def destroy(self):
+        self._graph = None
         if self.tp_ws is not None:
             self.tp_ws.close()
             self.tp_ws = None

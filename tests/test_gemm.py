@@ -111,3 +111,20 @@ def test_gemm_strided_views():
     C.gemm(a, False, b, False, D, C.EPI_F32)
     torch.cuda.synchronize()
     _check_close(D, a.float() @ b.float().t(), 1e-3)
+
+
+@pytest.mark.parametrize("M,N", [(8232, 832), (200, 96), (4096, 768)])
+def test_gemm_side_input_epilogues_ragged(M, N):
+    """RESID / DGELU epilogues read a side input one chunk ahead: ragged M/N and several tiles per CTA."""
+    C = _C()
+    K = 256
+    A, B, ref = _operands(M, N, K, False, False, seed=11)
+    R = torch.randn(M, N, device="cuda")
+    expect = R + ref
+    C.gemm(A, False, B, False, R, C.EPI_RESID, resid=R)
+    gp = torch.randn(M, N, device="cuda").bfloat16()
+    D2 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, False, B, False, D2, C.EPI_DGELU, aux=gp)
+    torch.cuda.synchronize()
+    _check_close(R, expect, 1e-3)
+    _check_close(D2, ref * gp.float(), 1e-2)

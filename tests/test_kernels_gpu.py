@@ -1,4 +1,6 @@
 """Numerics of the memory-bound sm_100a kernels against fp32 PyTorch references."""
+import time
+
 import pytest
 import torch
 
@@ -125,3 +127,31 @@ def test_gelu_math_matches_exact_erf_gelu():
     yr.backward(torch.ones_like(yr))
     assert (y.double() - yr).abs().max().item() < 2e-6
     assert (g.double() - xr.grad).abs().max().item() < 2e-6
+
+
+def test_peer_flag_wait_times_out_with_an_error_status():
+    """A cross-GPU flag wait whose flag is never set gives up after its limit, records
+    kErrPeerWait in the device error word and returns; the context stays usable."""
+    import mini_megatron_b200.ops as ops
+    C = ops.native()
+    C.clear_error()
+    flags = torch.zeros(8, dtype=torch.int32, device="cuda")     # nothing will ever raise these
+    slots = torch.zeros(4, 256, dtype=torch.bfloat16, device="cuda")
+    out = torch.full((4, 256), 7.0, device="cuda")
+    t0 = time.time()
+    C.tp_rs_reduce(slots.data_ptr(), slots.numel(), 1, flags.data_ptr(), 1, None, out, None, slots.numel(),
+                   timeout_ms=50)
+    torch.cuda.synchronize()
+    elapsed = time.time() - t0
+    assert C.get_error() == 301, C.get_error()
+    assert elapsed < 5.0
+    assert torch.all(out == 7.0)        # the kernel returned without touching the output
+    with pytest.raises(RuntimeError):
+        ops.check_errors()              # the host-side check turns the status into an exception
+    C.clear_error()
+    # the context is still usable
+    flags.fill_(1)
+    C.tp_rs_reduce(slots.data_ptr(), slots.numel(), 1, flags.data_ptr(), 1, None, out, None, slots.numel(),
+                   timeout_ms=50)
+    torch.cuda.synchronize()
+    assert C.get_error() == 0 and torch.all(out == 0.0)
