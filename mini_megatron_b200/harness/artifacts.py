@@ -56,15 +56,25 @@ def canonical_weights(model_config, seed) -> dict:
     return out
 
 
-def next_token_batches(num_batches, batch_size, seq_len, vocab, seed):
+def next_token_batches(num_batches, batch_size, seq_len, vocab, seed, pattern="next_token", effective_vocab=None):
+    """Fixed batches.  ``next_token``: uniform tokens, labels = the next token (last = -100);
+    ``shift``: labels = (token + 1) % effective_vocab (a learnable task); ``identity``: labels = tokens."""
     g = torch.Generator().manual_seed(seed)
-    tokens = torch.randint(0, vocab, (num_batches, batch_size, seq_len), generator=g, dtype=torch.long)
+    hi = effective_vocab or vocab
+    tokens = torch.randint(0, hi, (num_batches, batch_size, seq_len), generator=g, dtype=torch.long)
+    if pattern == "shift":
+        return tokens, (tokens + 1) % hi
+    if pattern == "identity":
+        return tokens, tokens.clone()
+    if pattern != "next_token":
+        raise ValueError(f"unknown pattern {pattern}")
     labels = torch.roll(tokens, -1, dims=-1)
     labels[..., -1] = -100
     return tokens, labels
 
 
-def freeze(out_dir, model_config, tp=1, pp=1, num_batches=64, batch_size=4, seed=20260818, padded_vocab=None):
+def freeze(out_dir, model_config, tp=1, pp=1, num_batches=64, batch_size=4, seed=20260818, padded_vocab=None,
+           pattern="next_token", effective_vocab=None):
     out_dir = Path(out_dir)
     if out_dir.exists():
         raise ValueError(f"refusing to overwrite artifact directory: {out_dir}")
@@ -91,14 +101,15 @@ def freeze(out_dir, model_config, tp=1, pp=1, num_batches=64, batch_size=4, seed
                 p = out_dir / f"reference_tp{tp}_pp{pp}_rank{rank}.pt"
                 torch.save(dict(meta, state_dict=shard_state(full, mc, tp, tp_rank, pp, pp_rank)), p)
                 files[f"reference_rank{rank}"] = p
-    tokens, labels = next_token_batches(num_batches, batch_size, mc["max_seq_len"], mc["vocab_size"], seed + 1)
+    tokens, labels = next_token_batches(num_batches, batch_size, mc["max_seq_len"], mc["vocab_size"], seed + 1,
+                                        pattern, effective_vocab)
     files["batches"] = out_dir / "next_token_batches.pt"
     torch.save({"schema_version": SCHEMA_VERSION, "contract": CONTRACT, "seed": seed + 1, "input_ids": tokens,
-                "labels": labels}, files["batches"])
+                "labels": labels, "pattern": pattern}, files["batches"])
     manifest = {"schema_version": SCHEMA_VERSION, "contract": CONTRACT, "seed": seed, "model": mc,
                 "topology": {"tp": tp, "pp": pp}, "padded_vocab": padded_vocab,
                 "reference_chunks": mc["vocab_size"] % tp == 0,
-                "batch_shape": list(tokens.shape),
+                "batch_shape": list(tokens.shape), "pattern": pattern, "effective_vocab": effective_vocab,
                 "files": {k: {"path": v.name, "sha256": sha256_file(v), "bytes": v.stat().st_size}
                           for k, v in files.items()}}
     (out_dir / "manifest.json").write_text(json.dumps(manifest, indent=2, sort_keys=True) + "\n", encoding="utf-8")
@@ -143,13 +154,16 @@ def main(argv=None):
     ap.add_argument("--batches", type=int, default=64)
     ap.add_argument("--batch-size", type=int, default=4)
     ap.add_argument("--seed", type=int, default=20260818)
+    ap.add_argument("--pattern", default="next_token", choices=("next_token", "shift", "identity"))
+    ap.add_argument("--effective-vocab", type=int, default=None)
     args = ap.parse_args(argv)
     from ..config import PRESETS
     mc = _model_dict(PRESETS[args.preset])
     if args.seq_len:
         mc["max_seq_len"] = args.seq_len
     try:
-        m = freeze(args.output_dir, mc, args.tp, args.pp, args.batches, args.batch_size, args.seed)
+        m = freeze(args.output_dir, mc, args.tp, args.pp, args.batches, args.batch_size, args.seed,
+                   pattern=args.pattern, effective_vocab=args.effective_vocab)
     except ValueError as exc:
         ap.error(str(exc))
     print(json.dumps(m, indent=2, sort_keys=True))
