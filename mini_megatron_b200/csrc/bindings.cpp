@@ -488,6 +488,48 @@ void tp_rs_reduce(int64_t slots_ptr, int64_t slot_stride, int64_t world, int64_t
                "tp_rs_reduce");
 }
 
+// lm_head GEMM whose epilogue also writes per-tile cross-entropy partials, then the
+// merge: returns (max, sumexp, target logit) per row like ce_fwd_stats.
+std::vector<Tensor> gemm_ce_stats(const Tensor& A, const Tensor& B, Tensor& D, const Tensor& labels,
+                                  int64_t vocab_start, int64_t n_valid) {
+  check_cuda(A, "A");
+  check_cuda(B, "B");
+  check_bf16(D, "D");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && A.size(1) == B.size(1), "gemm_ce_stats operands");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels must be contiguous int64");
+  const int64_t M = A.size(0), N = B.size(0), K = A.size(1);
+  TORCH_CHECK(D.size(0) == M && D.size(1) == N, "D shape");
+  const int64_t nparts = 2 * ((N + 255) / 256);
+  Tensor part = at::empty({M, nparts, 2}, A.options().dtype(at::kFloat));
+  mmb::GemmProblem p{};
+  p.A = A.data_ptr();
+  p.lda = A.stride(0);
+  p.B = B.data_ptr();
+  p.ldb = B.stride(0);
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.bn = 256;
+  p.num_sms = num_sms();
+  p.args.epi = mmb::EPI_CE_STATS;
+  p.args.alpha = 1.f;
+  p.args.err = error_word();
+  p.args.D = D.data_ptr();
+  p.args.ldd = D.stride(0);
+  p.args.ce_part = reinterpret_cast<float2*>(part.data_ptr<float>());
+  p.args.ce_ld = nparts;
+  p.args.ce_n_valid = (int)n_valid;
+  MMB_CHECK_RC(mmb::gemm_bf16_launch(p, cur_stream()), "gemm_ce_stats");
+  Tensor mx = at::empty({M}, A.options().dtype(at::kFloat));
+  Tensor se = at::empty_like(mx), tg = at::empty_like(mx);
+  MMB_CHECK_RC(mmb::ce_merge_stats(reinterpret_cast<const float2*>(part.data_ptr<float>()), nparts, (int)nparts,
+                                   reinterpret_cast<const __nv_bfloat16*>(D.data_ptr()), D.stride(0),
+                                   labels.data_ptr<int64_t>(), vocab_start, (int)n_valid, (int)M, mx.data_ptr<float>(),
+                                   se.data_ptr<float>(), tg.data_ptr<float>(), cur_stream()),
+               "ce_merge_stats");
+  return {mx, se, tg};
+}
+
 // GEMM with the TP collectives fused: optional all-gather wait on A rows and/or
 // reduce-scatter push epilogue (epi == EPI_PUSH_BF16, D unused).
 void gemm_tp(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const c10::optional<Tensor>& D, int64_t epi,
@@ -601,6 +643,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gamma"), py::arg("dres"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"),
         py::arg("dx_bf16") = c10::nullopt);
   m.def("ce_fwd_stats", &ce_fwd_stats);
+  m.def("gemm_ce_stats", &gemm_ce_stats, "lm_head GEMM with cross-entropy statistics fused into its epilogue");
   m.def("ce_bwd", &ce_bwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
@@ -624,6 +667,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("flags_ptr"), py::arg("epoch"), py::arg("resid"), py::arg("out"), py::arg("out_bf16"), py::arg("n"),
         py::arg("timeout_ms") = 10000);
   m.def("gemm_tp", &gemm_tp);
+  m.attr("EPI_CE_STATS") = (int)mmb::EPI_CE_STATS;
   m.attr("EPI_PUSH_BF16") = (int)mmb::EPI_PUSH_BF16;
   m.def("num_sms", &num_sms);
   m.def("flash_attn_fwd", &flash_attn_fwd);

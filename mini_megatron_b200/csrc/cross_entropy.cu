@@ -127,6 +127,47 @@ __global__ void __launch_bounds__(kCeThreads) ce_bwd_kernel(__nv_bfloat16* __res
   }
 }
 
+// Merges the per-tile (max, sumexp) partials that the lm_head GEMM epilogue
+// (EPI_CE_STATS) wrote, one warp per row, and gathers the target logit: the
+// forward statistics without re-reading the [rows, vocab] logits.
+__global__ void __launch_bounds__(256) ce_merge_kernel(const float2* __restrict__ part, long ld_part, int nparts,
+                                                       const __nv_bfloat16* __restrict__ logits, long ld,
+                                                       const long* __restrict__ labels, long vocab_start, int n_valid,
+                                                       int rows, float* __restrict__ out_max,
+                                                       float* __restrict__ out_sum, float* __restrict__ out_tgt) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float m = -INFINITY, s = 0.f;
+  const float2* pr = part + (size_t)row * ld_part;
+  for (int i = lane; i < nparts; i += 32) {
+    const float2 q = pr[i];
+    online_merge(m, s, q.x, q.y);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  if (lane == 0) {
+    out_max[row] = m;
+    out_sum[row] = s;
+    const long lab = labels[row] - vocab_start;
+    out_tgt[row] = (lab >= 0 && lab < n_valid) ? __bfloat162float(logits[(size_t)row * ld + lab]) : 0.f;
+  }
+}
+
+int ce_merge_stats(const float2* part, long ld_part, int nparts, const __nv_bfloat16* logits, long ld,
+                   const long* labels, long vocab_start, int n_valid, int rows, float* out_max, float* out_sum,
+                   float* out_tgt, cudaStream_t s) {
+  if (nparts < 1 || ld_part < nparts) return -1;
+  const int blocks = (rows * 32 + 255) / 256;
+  ce_merge_kernel<<<blocks, 256, 0, s>>>(part, ld_part, nparts, logits, ld, labels, vocab_start, n_valid, rows,
+                                         out_max, out_sum, out_tgt);
+  return (int)cudaGetLastError();
+}
+
 int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
                  float* out_max, float* out_sum, float* out_tgt, cudaStream_t s) {
   if ((ld % 8) != 0 || (reinterpret_cast<uintptr_t>(logits) & 15)) return -1;

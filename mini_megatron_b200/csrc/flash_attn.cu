@@ -248,19 +248,27 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
       if (!warp_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const bool diag = (j == qt);
-      // pass 1: row max of this tile (causal mask on the diagonal tile)
-      float mt = -INFINITY;
+      // pass 1: row max of this tile (causal mask on the diagonal tile).  Eight
+      // independent partial maxima keep the reduction off one serial chain.
+      float mx[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
 #pragma unroll
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_s + lane_off + cc * 32, v);
         tmem_wait_ld();
+        if (diag) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float s = __uint_as_float(v[e]);
-          if (!diag || cc * 32 + e <= r) mt = fmaxf(mt, s);
+          for (int e = 0; e < 32; ++e)
+            if (cc * 32 + e <= r) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(v[e]));
         }
       }
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float m_new = fmaxf(m, mt * sl2);
       const float alpha = exp2_approx(m - m_new);
       const int pb = j % C::P_BUFS;
@@ -268,8 +276,10 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
         ok = false;
         break;
       }
-      // pass 2: P = exp2(S*scale_log2 - m_new) -> bf16 -> swizzled smem
-      float rowsum = 0.f;
+      // pass 2: P = exp2(S*scale_log2 - m_new) -> bf16 -> swizzled smem (eight partial row sums)
+      float rs8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) rs8[k] = 0.f;
       uint8_t* prow = sP + pb * C::P_BYTES + r * 128;
 #pragma unroll
       for (int cc = 0; cc < BN / 32; ++cc) {
@@ -282,9 +292,11 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
           const int c0 = cc * 32 + e;
           float p0 = exp2_approx(__uint_as_float(v[e]) * sl2 - m_new);
           float p1 = exp2_approx(__uint_as_float(v[e + 1]) * sl2 - m_new);
-          if (diag && c0 > r) p0 = 0.f;
-          if (diag && c0 + 1 > r) p1 = 0.f;
-          rowsum += p0 + p1;
+          if (diag) {
+            if (c0 > r) p0 = 0.f;
+            if (c0 + 1 > r) p1 = 0.f;
+          }
+          rs8[(e >> 1) & 7] += p0 + p1;
           pk[e >> 1] = pack_bf16x2(p0, p1);
         }
         uint8_t* chunk = prow + (cc >> 1) * 16384;
@@ -299,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
       mbar_arrive(s_free);
       fence_proxy_async_smem();
       mbar_arrive(&p_full[pb]);
+      const float rowsum = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rowsum;
       m = m_new;
       if (j >= 1 && !accumulate_o(j - 1)) { ok = false; break; }

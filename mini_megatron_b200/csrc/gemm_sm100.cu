@@ -288,7 +288,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // chunks (128 bytes per row either way).  Warps w and w+4 share a TMEM lane
     // quarter and take alternate chunks, so two warps per scheduler run the
     // epilogue math.
-    constexpr bool OUT_BF16 = (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU || EPI == EPI_PUSH_BF16);
+    constexpr bool OUT_BF16 = (EPI == EPI_BF16 || EPI == EPI_GELU || EPI == EPI_DGELU || EPI == EPI_PUSH_BF16 ||
+                               EPI == EPI_CE_STATS);
     constexpr int W = OUT_BF16 ? 64 : 32;
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;   // which alternate chunks this warp takes
@@ -340,6 +341,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int rows_valid = min(32, args.M - r0);
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
       const int nchunks = BN / W;
+      float ce_m = -INFINITY, ce_s = 0.f;  // EPI_CE_STATS: this lane's row over this warp's chunks of the tile
 #pragma unroll 1
       for (int ch = half; ch < nchunks; ch += 2) {
         const int col0 = n0 + ch * W;
@@ -380,6 +382,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) =
                 make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
                            pack_bf16x2(v[8 * u + 4], v[8 * u + 5]), pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+        } else if constexpr (EPI == EPI_CE_STATS) {
+          // store the bf16 logits and fold this chunk's (max, sumexp) of the ROUNDED values into the row's
+          // running pair, so the statistics match the logits the backward reads
+          constexpr float kLog2e = 1.4426950408889634f;
+          const int nv = args.ce_n_valid - col0;  // valid columns in this chunk (may be <= 0 or >= 64)
+          float xb[W];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint4 w4 = make_uint4(pack_bf16x2(v[8 * u], v[8 * u + 1]), pack_bf16x2(v[8 * u + 2], v[8 * u + 3]),
+                                        pack_bf16x2(v[8 * u + 4], v[8 * u + 5]),
+                                        pack_bf16x2(v[8 * u + 6], v[8 * u + 7]));
+            *reinterpret_cast<uint4*>(stage_unit(stg, lane, u)) = w4;
+            const float2 f0 = unpack_bf16x2(w4.x), f1 = unpack_bf16x2(w4.y), f2 = unpack_bf16x2(w4.z),
+                         f3 = unpack_bf16x2(w4.w);
+            xb[8 * u + 0] = f0.x; xb[8 * u + 1] = f0.y; xb[8 * u + 2] = f1.x; xb[8 * u + 3] = f1.y;
+            xb[8 * u + 4] = f2.x; xb[8 * u + 5] = f2.y; xb[8 * u + 6] = f3.x; xb[8 * u + 7] = f3.y;
+          }
+          float cm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int i = 0; i < W; ++i)
+            if (i < nv) cm[i & 3] = fmaxf(cm[i & 3], xb[i]);
+          const float mc = fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3]));
+          if (mc > -INFINITY) {
+            float cs[4] = {0.f, 0.f, 0.f, 0.f};
+            const float mcl = mc * kLog2e;
+#pragma unroll
+            for (int i = 0; i < W; ++i)
+              if (i < nv) cs[i & 3] += fast_exp2(fmaf(xb[i], kLog2e, -mcl));
+            const float sc = (cs[0] + cs[1]) + (cs[2] + cs[3]);
+            if (mc > ce_m) {
+              ce_s = ce_s * fast_exp2((ce_m - mc) * kLog2e) + sc;
+              ce_m = mc;
+            } else {
+              ce_s += sc * fast_exp2((mc - ce_m) * kLog2e);
+            }
+          }
         } else if constexpr (EPI == EPI_GELU) {
           // gelu and gelu' share one erf evaluation; gelu' is stored (aux) for the backward
           uint32_t act[W / 2], grd[W / 2];
@@ -468,6 +506,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           bulk_commit();
         }
+      }
+      if constexpr (EPI == EPI_CE_STATS) {
+        if (lane < rows_valid)
+          args.ce_part[(size_t)(r0 + lane) * args.ce_ld + 2 * tn + half] = make_float2(ce_m, ce_s);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
@@ -559,6 +601,7 @@ static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, co
     case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU>(ta, tb, td, tx, args, grid, s);
     case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, td, tx, args, grid, s);
     case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, td, tx, args, grid, s);
+    case EPI_CE_STATS: return launch_one<BN, A_MN, B_MN, EPI_CE_STATS>(ta, tb, td, tx, args, grid, s);
     case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC>(ta, tb, td, tx, args, grid, s);
     case EPI_PUSH_BF16: return launch_one<BN, A_MN, B_MN, EPI_PUSH_BF16>(ta, tb, td, tx, args, grid, s);
   }
@@ -643,7 +686,10 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   if (rc) return rc - 30;
   // output (and GELU pre-activation) maps for the TMA-store epilogue
   CUtensorMap td, tx;
-  const bool out_bf16 = (args.epi == EPI_BF16 || args.epi == EPI_GELU || args.epi == EPI_DGELU);
+  const bool out_bf16 = (args.epi == EPI_BF16 || args.epi == EPI_GELU || args.epi == EPI_DGELU ||
+                         args.epi == EPI_CE_STATS);
+  if (args.epi == EPI_CE_STATS && (args.ce_part == nullptr || bn != 256 || args.ce_ld < 2L * ((p.N + 255) / 256)))
+    return -70;
   if (args.epi == EPI_PUSH_BF16) {
     // the epilogue writes peer slots with plain stores; this map only keeps the launch well-formed
     if (args.push_world < 1 || args.push_world > 8 || args.push_Sl % 32 != 0 || args.push_S % args.push_Sl != 0)

@@ -15,6 +15,8 @@ enum GemmEpilogue : int {
   EPI_DGELU = 5,    // D(bf16)  = alpha*acc * aux(bf16)          (aux = gelu'(pre) from EPI_GELU)
   EPI_F32_ATOMIC = 6,  // D(fp32) += alpha*acc with atomics (split-K partial sums)
   EPI_PUSH_BF16 = 7,   // bf16 tile -> owning TP rank's reduce-scatter slot (NVLink stores), then signal
+  EPI_CE_STATS = 8,    // D(bf16) = alpha*acc, plus per-row (max, sum exp(x - max)) of the stored bf16 values of
+                       // columns < ce_n_valid, one partial per (row, 256-column tile, epilogue half) in ce_part
 };
 
 struct GemmArgs {
@@ -39,6 +41,10 @@ struct GemmArgs {
   int* push_flags[8];
   int push_world, push_rank, push_epoch, push_S, push_Sl;
   unsigned* push_counter;
+  // cross-entropy statistics (EPI_CE_STATS): ce_part[row * ce_ld + 2 * n_tile + half] = (max, sumexp)
+  float2* ce_part;
+  long ce_ld;
+  int ce_n_valid;
 };
 
 struct GemmProblem {

@@ -47,6 +47,9 @@ int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const 
                  unsigned long long timeout_ns = 10000000000ull);
 int tp_ag_push(const __nv_bfloat16* src, int rows, int H, const AgPush& push, int num_sms, cudaStream_t s);
 
+int ce_merge_stats(const float2* part, long ld_part, int nparts, const __nv_bfloat16* logits, long ld,
+                   const long* labels, long vocab_start, int n_valid, int rows, float* out_max, float* out_sum,
+                   float* out_tgt, cudaStream_t s);
 int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
                  float* out_max, float* out_sum, float* out_tgt, cudaStream_t s);
 int ce_bwd(__nv_bfloat16* logits, long ld, int n_cols, const long* labels, long vocab_start, int n_valid, int rows,

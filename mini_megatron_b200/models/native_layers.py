@@ -24,6 +24,8 @@ parallelism, ``S`` otherwise.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -32,6 +34,9 @@ from ..ops import native
 from ..ops.attention import flash_attn_bwd, flash_attn_fwd
 from ..ops.linear import EPI_DGELU, EPI_RESID, linear_dgrad, linear_fwd, linear_gelu_fwd, linear_wgrad
 from ..parallel.param_buffer import bf16_weight, grad_target
+
+# Cross-entropy statistics from the lm_head GEMM epilogue (one fewer pass over the logits).
+_CE_FUSED = os.environ.get("MMB_CE_FUSED", "1") == "1"
 
 LN_EPS = 1e-5
 
@@ -288,13 +293,18 @@ class HeadLossFn(torch.autograd.Function):
         ln, m, r = _ln_fwd(x2, ln_f)
         ln_full = _gather_seq(ln, B, group) if sp else ln
         w = lm_head.weight
-        logits = linear_fwd(ln_full, bf16_weight(w))           # [B*S, V_local] bf16
         V_local = w.shape[0]
         tp_rank = dist.get_rank(group=group) if _world(group) > 1 else 0
         vstart = tp_rank * V_local
         n_valid = max(0, min(V_local, n_vocab - vstart))
         lab = labels.reshape(-1).contiguous()
-        mx, se, tg = native().ce_fwd_stats(logits, lab, vstart, n_valid)
+        if _CE_FUSED:
+            # the lm_head epilogue writes per-tile (max, sumexp) partials: no second pass over the logits
+            logits = torch.empty(ln_full.shape[0], V_local, device=x.device, dtype=torch.bfloat16)
+            mx, se, tg = native().gemm_ce_stats(ln_full, bf16_weight(w), logits, lab, vstart, n_valid)
+        else:
+            logits = linear_fwd(ln_full, bf16_weight(w))       # [B*S, V_local] bf16
+            mx, se, tg = native().ce_fwd_stats(logits, lab, vstart, n_valid)
         if _world(group) > 1:
             gmax = mx.clone()
             dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)

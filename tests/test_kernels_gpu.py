@@ -155,3 +155,32 @@ def test_peer_flag_wait_times_out_with_an_error_status():
                    timeout_ms=50)
     torch.cuda.synchronize()
     assert C.get_error() == 0 and torch.all(out == 0.0)
+
+
+@pytest.mark.parametrize("M,N,n_valid", [(512, 1024, 1000), (300, 50304, 50257), (128, 256, 256)])
+def test_lm_head_gemm_with_fused_ce_statistics(M, N, n_valid):
+    """gemm_ce_stats: bf16 logits identical to the plain GEMM, and (max, sumexp, target) equal to the
+    standalone statistics pass over those logits (fp32 PyTorch reference on the stored bf16 values)."""
+    import mini_megatron_b200.ops as ops
+    C = ops.native()
+    torch.manual_seed(0)
+    K = 256
+    A = (torch.randn(M, K, device="cuda") * 0.5).bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.5).bfloat16()
+    lab = torch.randint(0, n_valid, (M,), device="cuda")
+    lab[::7] = -100
+    D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    mx, se, tg = C.gemm_ce_stats(A, B, D, lab, 0, n_valid)
+    D2 = torch.empty_like(D)
+    C.gemm(A, False, B, False, D2, C.EPI_BF16)
+    torch.cuda.synchronize()
+    assert torch.equal(D, D2)
+    x = D.float()[:, :n_valid]
+    ref_max = x.max(dim=1).values
+    ref_lse = torch.logsumexp(x, dim=1)
+    assert torch.allclose(mx, ref_max)
+    assert torch.allclose(mx + torch.log(se), ref_lse, atol=1e-4, rtol=1e-5)
+    ok = lab >= 0
+    ref_tg = torch.zeros(M, device="cuda")
+    ref_tg[ok] = x[ok].gather(1, lab[ok].unsqueeze(1)).squeeze(1)
+    assert torch.equal(tg, ref_tg)

@@ -127,3 +127,29 @@ def test_cuda_graph_step_matches_eager():
         # magnifies that noise on small vectors (LayerNorm biases ~5e-3): judge those by absolute error
         ref = eager[1][k]
         assert _rel(v, ref) < 2e-3 or (v - ref).abs().max().item() < 1e-4, (k, _rel(v, ref))
+
+
+def test_fused_ce_statistics_match_the_two_pass_head(monkeypatch):
+    """The head with cross-entropy statistics from the lm_head epilogue gives the same loss and
+    gradients as the separate statistics pass."""
+    from mini_megatron_b200.config import GPTConfig
+    from mini_megatron_b200.models import native_layers
+    from mini_megatron_b200.models.loss import CrossEntropyLoss  # noqa: F401
+    from mini_megatron_b200.training import synthetic_batch
+    cfg = GPTConfig(num_layers=1, hidden_size=256, num_attention_heads=4, ffn_hidden_size=1024, max_seq_len=256,
+                    vocab_size=1000)
+    tok, lab = synthetic_batch(1, 2, 256, 1000, seed=3)
+    tok, lab = tok[0].cuda(), lab[0].cuda()
+    out = {}
+    for fused in (False, True):
+        monkeypatch.setattr(native_layers, "_CE_FUSED", fused)
+        model = _model(cfg).cuda()
+        from mini_megatron_b200.optim import make_param_buffer
+        make_param_buffer(model)
+        _, loss = model(tok, lab, torch.ones(2, 256, device="cuda"))
+        loss.backward()
+        out[fused] = (loss.item(), {n: (getattr(p, "main_grad", None) if getattr(p, "main_grad", None) is not None
+                                        else p.grad).detach().clone() for n, p in model.named_parameters()})
+    assert abs(out[True][0] - out[False][0]) < 1e-4 * abs(out[False][0])
+    for n, g in out[True][1].items():
+        assert _rel(g, out[False][1][n]) < 1e-3, n
