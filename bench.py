@@ -54,7 +54,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "GPT train tok/s (device-timed, max over ranks) at 1/2/4/8 B200 vs ref's NCCL"
 MODEL = dict(num_layers=12, hidden_size=768, num_attention_heads=12, ffn_hidden_size=3072, max_seq_len=1024,
              vocab_size=50257)
-BASELINE_VALUE = None  # BASELINE.md publishes no B200 number for this config
+BASELINE_VALUE = None  # the reference publishes no B200 number for this config
 M_1_3B = dict(num_layers=24, hidden_size=2048, num_attention_heads=16, ffn_hidden_size=8192, max_seq_len=2048,
               vocab_size=50257)
 M_6_7B = dict(num_layers=32, hidden_size=4096, num_attention_heads=32, ffn_hidden_size=16384, max_seq_len=2048,

@@ -124,7 +124,7 @@ def test_cuda_graph_step_matches_eager():
         assert abs(a - b) < 2e-3 * abs(a), (eager[0], graph[0])
     for k, v in graph[1].items():
         # split-K and atomic reductions leave the summation order open, and Adam's normalisation
-        # magnifies that noise on small vectors (LayerNorm biases ~5e-3): judge those by absolute error
+        # magnifies that noise on small vectors (LayerNorm biases ~5e-3): compare those by absolute error
         ref = eager[1][k]
         assert _rel(v, ref) < 2e-3 or (v - ref).abs().max().item() < 1e-4, (k, _rel(v, ref))
 
