@@ -245,6 +245,12 @@ class DecoderLayerFn(torch.autograd.Function):
         return (out, None, None, None, None) + (None,) * ctx.n_params
 
 
+def run_grad_ready_hooks(module):
+    """Tell the data-parallel gradient sync that ``module``'s gradients are final (its backward was enqueued)."""
+    for hook in getattr(module, "_mmb_grad_ready_hooks", ()):
+        hook()
+
+
 class EmbeddingFn(torch.autograd.Function):
     """x = tok_emb(ids) (vocab-parallel, TP-summed) + pos_emb; SP keeps the local sequence shard."""
 
@@ -279,6 +285,7 @@ class EmbeddingFn(torch.autograd.Function):
         native().embedding_bwd(ids.view(-1), d2, grad_target(tok.weight),
                                grad_target(pos.weight) if pos.weight.requires_grad else None, B, S,
                                tok.vocab_start_index, tok.vocab_end_index)
+        run_grad_ready_hooks(emb)
         return (None, None, None, None) + (None,) * ctx.n_params
 
 
@@ -338,6 +345,8 @@ class HeadLossFn(torch.autograd.Function):
         if _world(ctx.group) > 1:
             d_ln = _reduce(d_ln, ctx.B, ctx.group, ctx.sp)
         dx = _ln_bwd(d_ln, x2, m, r, ctx.ln_f, want_bf16=True)
+        run_grad_ready_hooks(ctx.lm_head)
+        run_grad_ready_hooks(ctx.ln_f)
         out = dx.view(ctx.x_shape)
         out._mmb_bf16 = dx._mmb_bf16.view(ctx.x_shape)
         return (out, None, None, None, None, None, None, None) + (None,) * ctx.n_params

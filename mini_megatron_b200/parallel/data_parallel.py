@@ -58,8 +58,10 @@ class GradSync:
 
     def attach(self, modules):
         """Mark a module's parameters ready when its native backward finishes."""
+        self.attached_params = getattr(self, "attached_params", set())
         for m in modules:
             params = [p for p in m.parameters() if id(p) in self._bucket_of]
+            self.attached_params.update(id(p) for p in params)
             hooks = list(getattr(m, "_mmb_grad_ready_hooks", ()))
             hooks.append(lambda ps=params: self.mark_ready(ps))
             m._mmb_grad_ready_hooks = hooks

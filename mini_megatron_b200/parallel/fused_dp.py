@@ -96,8 +96,10 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         self._launched_step = False
 
     def attach(self, modules):
+        self.attached_params = getattr(self, "attached_params", set())
         for m in modules:
             params = [p for p in m.parameters() if id(p) in self._bucket_of]
+            self.attached_params.update(id(p) for p in params)
             hooks = list(getattr(m, "_mmb_grad_ready_hooks", ()))
             hooks.append(lambda ps=params: self.mark_ready(ps))
             m._mmb_grad_ready_hooks = hooks

@@ -100,6 +100,7 @@ class TrainConfig:
     average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
     seed: int = 42
     nvtx: bool = False                  # NVTX ranges per phase (also MMB_NVTX=1)
+    dp_early_buckets: bool = False      # launch DP buckets during backward (also MMB_DP_EARLY_BUCKETS=1)
     cuda_graph: str = "auto"            # "on", "off", or "auto": replay each whole step as one CUDA graph
                                         # where supported (CUDA, tp = pp = dp = 1, flat fused AdamW)
 
@@ -170,7 +171,16 @@ class Trainer:
             for i, layer in enumerate(layers):
                 layer._mmb_tp_ws = self.tp_ws
                 layer._mmb_tp_slot = i
-        self.grad_sync.attach(list(layers))
+        # Modules whose native backward announces "gradients final".  DP buckets launch strictly in
+        # order, head first, so the head and the embedding must be attached as well for any bucket to
+        # start during backward (MMB_DP_EARLY_BUCKETS=1; otherwise buckets start after backward).
+        ready = list(layers)
+        if cfg.dp_early_buckets or os.environ.get("MMB_DP_EARLY_BUCKETS") == "1":
+            for name in ("embedding", "ln_f", "lm_head"):
+                mod = getattr(self.model, name, None)
+                if mod is not None:
+                    ready.append(mod)
+        self.grad_sync.attach(ready)
         self.scheduler = torch.optim.lr_scheduler.LambdaLR(self.optimizer,
                                                            make_lr_lambda(cfg.warmup_steps, cfg.num_steps))
         self.sp_params = [p for p in self.model.parameters() if getattr(p, "sequence_parallel_grad", False)]

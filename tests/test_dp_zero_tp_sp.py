@@ -162,3 +162,40 @@ def _load_expected(shard, ref, rank, world, like):
             shard[k] = f[:, rank * n:(rank + 1) * n]
         else:
             shard[k] = f
+
+
+def _overlap_worker(rank, world):
+    """Grad-ready hooks fired in backward order launch the DP buckets progressively (before finish)."""
+    from mini_megatron_b200.config import GPTConfig
+    from mini_megatron_b200.models import build_gpt
+    from mini_megatron_b200.models.native_layers import run_grad_ready_hooks
+    from mini_megatron_b200.optim import make_param_buffer
+    from mini_megatron_b200.parallel import process_groups as pg
+    from mini_megatron_b200.parallel.data_parallel import GradSync
+    mpu = pg.init_model_parallel(1, 1)
+    pg.set_model_parallel(mpu)
+    torch.manual_seed(0)
+    model = build_gpt(GPTConfig(**CFG))
+    buf = make_param_buffer(model, align=world, bucket_elems=20000)
+    gs = GradSync(buf, mpu["dp_group"], mode="allreduce", overlap=True)
+    order = [model.lm_head, model.ln_f] + list(reversed(model.decoder.layers)) + [model.embedding]
+    gs.attach(order)
+    assert gs.attached_params == {id(p) for p in buf.params}
+    launched = []
+    for m in order:
+        run_grad_ready_hooks(m)
+        launched.append(len(gs._works))
+    n_buckets = len(buf.buckets)
+    gs.finish()
+    pg.set_model_parallel(None)
+    return {"launched": launched, "n_buckets": n_buckets}
+
+
+def test_grad_ready_hooks_launch_buckets_during_backward():
+    res = run_ranks(_overlap_worker, 2)
+    for r in res:
+        launched, n = r["launched"], r["n_buckets"]
+        assert n >= 3
+        assert launched == sorted(launched)            # in order, never retracted
+        assert launched[0] >= 1                        # the head's bucket goes out right after the head
+        assert launched[-1] == n                       # every bucket launched before finish()

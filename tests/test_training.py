@@ -3,6 +3,7 @@ import os
 import subprocess
 import sys
 
+import pytest
 import torch
 
 from mini_megatron_b200 import config as cfg
@@ -82,3 +83,21 @@ def test_cli_runs_pp2_tp1_dp1_on_gloo(tmp_path):
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-4000:]
     assert "Throughput:" in out.stdout and "step    2 | loss" in out.stdout
     assert (tmp_path / "ck" / "manifest.json").exists()
+
+
+@pytest.mark.parametrize("pp", [1])
+def test_trainer_attaches_every_parameter_to_a_grad_ready_hook(pp):
+    """DP buckets launch strictly in order during backward, so every parameter of the
+    chunk must belong to a module whose backward announces its gradients."""
+    import torch.distributed as dist
+    from mini_megatron_b200.config import PRESETS
+    from mini_megatron_b200.parallel import process_groups as pg
+    from mini_megatron_b200.training import TrainConfig, Trainer
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29588")
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    t = Trainer(TrainConfig(model=PRESETS["tiny"], micro_batch_size=2, seq_len=32, pp=pp, dp_early_buckets=True),
+                device="cpu")
+    assert t.grad_sync.attached_params == {id(p) for p in t.buf.params}
+    pg.set_model_parallel(None)
