@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
                                                     float b2, float eps, float wd, float step_size,
                                                     float bc2_sqrt, float grad_scale,
                                                     const float* __restrict__ hyper) {
+  pdl_trigger();
+  pdl_wait();
   if (hyper) {  // step-dependent scalars from device memory (CUDA-graph replays)
     lr = hyper[0];
     step_size = hyper[1];
@@ -77,6 +79,8 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
 // hyper = {lr, lr / (1 - b1^step), sqrt(1 - b2^step)}.
 __global__ void adamw_hyper_kernel(int* __restrict__ step, const float* __restrict__ lr_table, int n_table, double b1,
                                    double b2, float* __restrict__ hyper) {
+  pdl_trigger();
+  pdl_wait();
   if (blockIdx.x != 0 || threadIdx.x != 0) return;
   const int s = *step + 1;
   *step = s;
@@ -89,11 +93,13 @@ __global__ void adamw_hyper_kernel(int* __restrict__ step, const float* __restri
 int adamw_hyper_step(int* step, const float* lr_table, int n_table, double b1, double b2, float* hyper,
                      cudaStream_t s) {
   if (n_table < 1) return -1;
-  adamw_hyper_kernel<<<1, 32, 0, s>>>(step, lr_table, n_table, b1, b2, hyper);
+  launch_k(adamw_hyper_kernel, 1, 32, 0, s, step, lr_table, n_table, b1, b2, hyper);
   return (int)cudaGetLastError();
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long n) {
+  pdl_trigger();
+  pdl_wait();
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     y[i] = __float2bfloat16(x[i]);
 }
@@ -107,14 +113,14 @@ int adamw_flat(float* p, const float* g, float* m, float* v, __nv_bfloat16* pb, 
   if (pb && (reinterpret_cast<uintptr_t>(pb) & 7)) return -2;
   const long n4 = (n + 3) / 4;
   const int blocks = (int)std::min<long>((n4 + 255) / 256, (long)num_sms * 8);
-  adamw_kernel<<<std::max(blocks, 1), 256, 0, s>>>(p, g, m, v, pb, n, lr, b1, b2, eps, wd, step_size, bc2_sqrt,
+  launch_k(adamw_kernel, std::max(blocks, 1), 256, 0, s, p, g, m, v, pb, n, lr, b1, b2, eps, wd, step_size, bc2_sqrt,
                                                    grad_scale, hyper);
   return (int)cudaGetLastError();
 }
 
 int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStream_t s) {
   const int blocks = (int)std::min<long>((n + 255) / 256, (long)num_sms * 8);
-  f32_to_bf16_kernel<<<std::max(blocks, 1), 256, 0, s>>>(x, y, n);
+  launch_k(f32_to_bf16_kernel, std::max(blocks, 1), 256, 0, s, x, y, n);
   return (int)cudaGetLastError();
 }
 
@@ -124,6 +130,8 @@ namespace mmb {
 
 // y = gelu(x), g = gelu'(x) in fp32 (the epilogue math, exposed for accuracy checks)
 __global__ void gelu_fwd_bwd_kernel(const float* __restrict__ x, float* __restrict__ y, float* __restrict__ g, long n) {
+  pdl_trigger();
+  pdl_wait();
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     y[i] = gelu_f(x[i]);
     g[i] = gelu_grad_f(x[i]);
@@ -132,7 +140,7 @@ __global__ void gelu_fwd_bwd_kernel(const float* __restrict__ x, float* __restri
 
 int gelu_fwd_bwd_f32(const float* x, float* y, float* g, long n, int num_sms, cudaStream_t s) {
   const int blocks = (int)std::min<long>((n + 255) / 256, (long)num_sms * 8);
-  gelu_fwd_bwd_kernel<<<std::max(blocks, 1), 256, 0, s>>>(x, y, g, n);
+  launch_k(gelu_fwd_bwd_kernel, std::max(blocks, 1), 256, 0, s, x, y, g, n);
   return (int)cudaGetLastError();
 }
 

@@ -5,6 +5,8 @@
 // issuing CTA's own shared memory only), tcgen05 MMA / TMEM allocation / TMEM loads, and the
 // shared-memory matrix descriptor used by tcgen05.mma.
 #pragma once
+#include <cstdlib>
+#include <utility>
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -32,6 +34,49 @@ constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// With MMB_PDL=1 every kernel of this package is launched with programmatic
+// stream serialisation: the next kernel on the stream may be scheduled as soon
+// as every CTA of the current one has started, so its prologue (barrier
+// init, TMEM allocation, descriptor prefetch) overlaps the tail of its
+// predecessor.  Each kernel calls pdl_wait() before its first global-memory
+// access, which blocks until the previous grid has completed and its writes
+// are visible, so the data dependencies are those of plain stream order.
+// Both instructions are no-ops for a grid launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MMB_PDL");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
+// Kernel launch: a plain stream-ordered launch, or, with MMB_PDL=1, cudaLaunchKernelEx
+// with the programmatic-serialisation attribute.  Errors are left for the caller's
+// cudaGetLastError().
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args&&... args) {
+  if (!pdl_enabled()) {
+    kernel<<<grid, block, smem, stream>>>(std::forward<Args>(args)...);
+    return cudaPeekAtLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // 2^x with the hardware approximation (ex2.approx; -inf -> 0).

@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const __nv_bfloat16*
                                                             const long* __restrict__ labels, long vocab_start,
                                                             int n_valid, float* __restrict__ out_max,
                                                             float* __restrict__ out_sum, float* __restrict__ out_tgt) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const __nv_bfloat16* x = logits + (size_t)row * ld;
   float m = -INFINITY, s = 0.f;
@@ -97,6 +99,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_bwd_kernel(__nv_bfloat16* __res
                                                             const long* __restrict__ labels, long vocab_start,
                                                             int n_valid, const float* __restrict__ lse,
                                                             const float* __restrict__ scale) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   __nv_bfloat16* x = logits + (size_t)row * ld;
   const float l = lse[row];
@@ -135,6 +139,8 @@ __global__ void __launch_bounds__(256) ce_merge_kernel(const float2* __restrict_
                                                        const long* __restrict__ labels, long vocab_start, int n_valid,
                                                        int rows, float* __restrict__ out_max,
                                                        float* __restrict__ out_sum, float* __restrict__ out_tgt) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -163,7 +169,7 @@ int ce_merge_stats(const float2* part, long ld_part, int nparts, const __nv_bflo
                    float* out_tgt, cudaStream_t s) {
   if (nparts < 1 || ld_part < nparts) return -1;
   const int blocks = (rows * 32 + 255) / 256;
-  ce_merge_kernel<<<blocks, 256, 0, s>>>(part, ld_part, nparts, logits, ld, labels, vocab_start, n_valid, rows,
+  launch_k(ce_merge_kernel, blocks, 256, 0, s, part, ld_part, nparts, logits, ld, labels, vocab_start, n_valid, rows,
                                          out_max, out_sum, out_tgt);
   return (int)cudaGetLastError();
 }
@@ -171,14 +177,14 @@ int ce_merge_stats(const float2* part, long ld_part, int nparts, const __nv_bflo
 int ce_fwd_stats(const __nv_bfloat16* logits, long ld, const long* labels, long vocab_start, int n_valid, int rows,
                  float* out_max, float* out_sum, float* out_tgt, cudaStream_t s) {
   if ((ld % 8) != 0 || (reinterpret_cast<uintptr_t>(logits) & 15)) return -1;
-  ce_fwd_kernel<<<rows, kCeThreads, 0, s>>>(logits, ld, labels, vocab_start, n_valid, out_max, out_sum, out_tgt);
+  launch_k(ce_fwd_kernel, rows, kCeThreads, 0, s, logits, ld, labels, vocab_start, n_valid, out_max, out_sum, out_tgt);
   return (int)cudaGetLastError();
 }
 
 int ce_bwd(__nv_bfloat16* logits, long ld, int n_cols, const long* labels, long vocab_start, int n_valid, int rows,
            const float* lse, const float* scale, cudaStream_t s) {
   if ((ld % 8) != 0 || (reinterpret_cast<uintptr_t>(logits) & 15)) return -1;
-  ce_bwd_kernel<<<rows, kCeThreads, 0, s>>>(logits, ld, n_cols, labels, vocab_start, n_valid, lse, scale);
+  launch_k(ce_bwd_kernel, rows, kCeThreads, 0, s, logits, ld, n_cols, labels, vocab_start, n_valid, lse, scale);
   return (int)cudaGetLastError();
 }
 

@@ -16,6 +16,8 @@ namespace mmb {
 __global__ void emb_fwd_kernel(const long* __restrict__ ids, const float* __restrict__ wte,
                                const float* __restrict__ wpe, float* __restrict__ out, int rows, int H, int S,
                                long vstart, long vend) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -36,6 +38,8 @@ __global__ void emb_fwd_kernel(const long* __restrict__ ids, const float* __rest
 
 __global__ void emb_bwd_tok_kernel(const long* __restrict__ ids, const float* __restrict__ dout,
                                    float* __restrict__ dwte, int rows, int H, long vstart, long vend) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -47,6 +51,8 @@ __global__ void emb_bwd_tok_kernel(const long* __restrict__ ids, const float* __
 }
 
 __global__ void emb_bwd_pos_kernel(const float* __restrict__ dout, float* __restrict__ dwpe, int B, int S, int H) {
+  pdl_trigger();
+  pdl_wait();
   const int s = blockIdx.x;
   for (int c = threadIdx.x; c < H; c += blockDim.x) {
     float acc = 0.f;
@@ -58,7 +64,7 @@ __global__ void emb_bwd_pos_kernel(const float* __restrict__ dout, float* __rest
 int embedding_fwd(const long* ids, const float* wte, const float* wpe, float* out, int rows, int H, int S,
                   long vstart, long vend, cudaStream_t s) {
   if (H % 4) return -1;
-  emb_fwd_kernel<<<(rows * 32 + 255) / 256, 256, 0, s>>>(ids, wte, wpe, out, rows, H, S, vstart, vend);
+  launch_k(emb_fwd_kernel, (rows * 32 + 255) / 256, 256, 0, s, ids, wte, wpe, out, rows, H, S, vstart, vend);
   return (int)cudaGetLastError();
 }
 
@@ -66,8 +72,8 @@ int embedding_bwd(const long* ids, const float* dout, float* dwte, float* dwpe, 
                   long vend, cudaStream_t s) {
   if (H % 4) return -1;
   const int rows = B * S;
-  emb_bwd_tok_kernel<<<(rows * 32 + 255) / 256, 256, 0, s>>>(ids, dout, dwte, rows, H, vstart, vend);
-  if (dwpe) emb_bwd_pos_kernel<<<S, 256, 0, s>>>(dout, dwpe, B, S, H);
+  launch_k(emb_bwd_tok_kernel, (rows * 32 + 255) / 256, 256, 0, s, ids, dout, dwte, rows, H, vstart, vend);
+  if (dwpe) launch_k(emb_bwd_pos_kernel, S, 256, 0, s, dout, dwpe, B, S, H);
   return (int)cudaGetLastError();
 }
 

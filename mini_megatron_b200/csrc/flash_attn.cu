@@ -81,6 +81,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
 template <int D>
 __global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const FwdArgs a) {
+  pdl_trigger();
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, FwdCfg<D>::MIN_CTAS)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // set-up above touched no global memory
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_s = tmem;            // S: columns [0, 128)
   const uint32_t t_o = tmem + BN;       // O buffers: [128, 128 + 2D)
@@ -373,7 +375,7 @@ int flash_attn_fwd(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, int nh, 
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdCfg<64>::SMEM);
       set = true;
     }
-    k<<<grid, kThreads, FwdCfg<64>::SMEM, stream>>>(tm, a);
+    launch_k(k, grid, kThreads, FwdCfg<64>::SMEM, stream, tm, a);
   } else {
     auto k = flash_fwd_kernel<128>;
     static bool set = false;
@@ -381,7 +383,7 @@ int flash_attn_fwd(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, int nh, 
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdCfg<128>::SMEM);
       set = true;
     }
-    k<<<grid, kThreads, FwdCfg<128>::SMEM, stream>>>(tm, a);
+    launch_k(k, grid, kThreads, FwdCfg<128>::SMEM, stream, tm, a);
   }
   return (int)cudaGetLastError();
 }
@@ -448,6 +450,7 @@ template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_dq, const BwdArgs a) {
+  pdl_trigger();
   using C = BwdCfg<D>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -512,6 +515,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // set-up above touched no global memory
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -737,6 +741,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // One thread per 8 elements (16 bytes); the D/8 threads of a (row, head) reduce with shuffles.
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
                                   long ld, int B, int S, int nh, int D, float* __restrict__ delta) {
+  pdl_trigger();
+  pdl_wait();
   const int g = D / 8;  // threads per (row, head): 8 or 16
   const long tid = blockIdx.x * (long)blockDim.x + threadIdx.x;
   const long pair = tid / g;  // (row, head) index
@@ -768,6 +774,8 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const 
 // dqkv[:, q block] = bf16(dq_acc)
 __global__ void attn_dq_convert_kernel(const float* __restrict__ dq, long ld_dq, __nv_bfloat16* __restrict__ dqkv,
                                        long ld_dqkv, long rows, int width) {
+  pdl_trigger();
+  pdl_wait();
   const long n4 = rows * (width / 4);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
     const long r = i / (width / 4), c = (i % (width / 4)) * 4;
@@ -792,7 +800,7 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
   // Delta = rowsum(dO * O)
   {
     const long threads = rows * nh * (d / 8);
-    attn_delta_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(dout, out, ld_do, B, S, nh, d, delta);
+    launch_k(attn_delta_kernel, (unsigned)((threads + 255) / 256), 256, 0, stream, dout, out, ld_do, B, S, nh, d, delta);
   }
   cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * nh * d, stream);
   CUtensorMap tm_qkv, tm_do;
@@ -827,7 +835,7 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<64>::SMEM);
       set = true;
     }
-    k<<<grid, kBwdThreads, BwdCfg<64>::SMEM, stream>>>(tm_qkv, tm_do, tm_dq, a);
+    launch_k(k, grid, kBwdThreads, BwdCfg<64>::SMEM, stream, tm_qkv, tm_do, tm_dq, a);
   } else {
     auto k = flash_bwd_kernel<128>;
     static bool set = false;
@@ -835,10 +843,10 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
       cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdCfg<128>::SMEM);
       set = true;
     }
-    k<<<grid, kBwdThreads, BwdCfg<128>::SMEM, stream>>>(tm_qkv, tm_do, tm_dq, a);
+    launch_k(k, grid, kBwdThreads, BwdCfg<128>::SMEM, stream, tm_qkv, tm_do, tm_dq, a);
   }
   const long n4 = rows * nh * d / 4;
-  attn_dq_convert_kernel<<<(unsigned)std::min<long>((n4 + 255) / 256, (long)num_sms * 8), 256, 0, stream>>>(
+  launch_k(attn_dq_convert_kernel, (unsigned)std::min<long>((n4 + 255) / 256, (long)num_sms * 8), 256, 0, stream, 
       dq_acc, (long)nh * d, dqkv, ld_dqkv, rows, nh * d);
   return (int)cudaGetLastError();
 }

@@ -77,6 +77,8 @@ __device__ bool wait_flags(const int* pad, int slot, int world, int epoch, int* 
 }
 
 __global__ void __launch_bounds__(256) dp_rs_adamw_ag_kernel(const DpPeers P, const DpArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int world = a.world;
   const int slot_ready = a.bucket * 2, slot_done = a.bucket * 2 + 1;
   // 1. publish "my gradients of this bucket are final" (written by earlier kernels on this stream)
@@ -175,7 +177,7 @@ int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t s
   a.err = s.err;
   const long n4 = (s.hi - s.lo) / 4;
   const int blocks = (int)std::max<long>(1, std::min<long>((n4 + 255) / 256, s.max_ctas));
-  dp_rs_adamw_ag_kernel<<<blocks, 256, 0, stream>>>(P, a);
+  launch_k(dp_rs_adamw_ag_kernel, blocks, 256, 0, stream, P, a);
   return (int)cudaGetLastError();
 }
 

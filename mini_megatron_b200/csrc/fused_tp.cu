@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(256) tp_rs_reduce_kernel(const __nv_bfloat16* 
                                                            const float* __restrict__ resid, float* __restrict__ out,
                                                            __nv_bfloat16* __restrict__ out_bf16, long n, int* err,
                                                            unsigned long long timeout_ns) {
+  pdl_trigger();
+  pdl_wait();
   if (!cta_wait_flags(flags, world, epoch, err, timeout_ns)) return;
   const long n8 = n >> 3;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
@@ -72,6 +74,8 @@ __global__ void __launch_bounds__(256) tp_rs_reduce_kernel(const __nv_bfloat16* 
 // kernel is not one of ours, e.g. a gradient handed in by autograd).
 __global__ void __launch_bounds__(256) tp_ag_push_kernel(const __nv_bfloat16* __restrict__ src, int rows, int H,
                                                          const AgPush P) {
+  pdl_trigger();
+  pdl_wait();
   const int units = H / 8;
   const long n = (long)rows * units;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
@@ -89,7 +93,7 @@ int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const 
                  cudaStream_t s, unsigned long long timeout_ns) {
   if (n % 8 != 0 || world < 1 || world > 8 || slot_stride % 8 != 0) return -1;
   const int blocks = (int)std::max<long>(1, std::min<long>((n / 8 + 255) / 256, (long)num_sms * 4));
-  tp_rs_reduce_kernel<<<blocks, 256, 0, s>>>(slots, slot_stride, world, flags, epoch, resid, out, out_bf16, n, err,
+  launch_k(tp_rs_reduce_kernel, blocks, 256, 0, s, slots, slot_stride, world, flags, epoch, resid, out, out_bf16, n, err,
                                              timeout_ns);
   return (int)cudaGetLastError();
 }
@@ -98,7 +102,7 @@ int tp_ag_push(const __nv_bfloat16* src, int rows, int H, const AgPush& push, in
   if (H % 8 != 0 || push.world < 1 || push.world > 8) return -1;
   const long n = (long)rows * (H / 8);
   const int blocks = (int)std::max<long>(1, std::min<long>((n + 255) / 256, (long)num_sms * 4));
-  tp_ag_push_kernel<<<blocks, 256, 0, s>>>(src, rows, H, push);
+  launch_k(tp_ag_push_kernel, blocks, 256, 0, s, src, rows, H, push);
   return (int)cudaGetLastError();
 }
 

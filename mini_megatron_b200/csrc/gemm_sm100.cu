@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmAux,
                     const GemmArgs args) {
+  pdl_trigger();
   using C = GemmCfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // set-up above touched no global memory; everything below may depend on the previous kernel
 
   const int mtiles = (args.M + BM - 1) / BM;
   const int ntiles = (args.N + BN - 1) / BN;
@@ -587,7 +589,7 @@ static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, cons
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  kern<<<grid, kGemmThreads, smem, stream>>>(ta, tb, td, tx, args);
+  launch_k(kern, grid, kGemmThreads, smem, stream, ta, tb, td, tx, args);
   return cudaGetLastError();
 }
 

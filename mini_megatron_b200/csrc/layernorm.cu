@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
                                                      const float* __restrict__ beta, __nv_bfloat16* __restrict__ y,
                                                      float* __restrict__ mean_out, float* __restrict__ rstd_out,
                                                      int rows, int H, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -79,6 +81,8 @@ __global__ void __launch_bounds__(256) ln_fwd_push_kernel(const float* __restric
                                                           const float* __restrict__ beta, float* __restrict__ mean_out,
                                                           float* __restrict__ rstd_out, int rows, int H, float eps,
                                                           const AgPush P) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   const int nvec = H >> 2;
@@ -139,6 +143,8 @@ __global__ void __launch_bounds__(256, NV <= 6 ? 3 : 1) ln_bwd_kernel(const __nv
                                                      const float* __restrict__ gamma, const float* __restrict__ dres,
                                                      float* __restrict__ dx, __nv_bfloat16* __restrict__ dx_bf16,
                                                      float* __restrict__ part, int rows, int H, const AgPush P = AgPush{}) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -250,6 +256,8 @@ __global__ void __launch_bounds__(256) ln_param_part_kernel(const __nv_bfloat16*
                                                             const float* __restrict__ x, const float* __restrict__ mean,
                                                             const float* __restrict__ rstd, float* __restrict__ part,
                                                             int rows, int H, int rows_per_band) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.y * blockDim.x + threadIdx.x;
   if (c >= H) return;
   const int r0 = blockIdx.x * rows_per_band, r1 = min(rows, r0 + rows_per_band);
@@ -269,6 +277,8 @@ __global__ void __launch_bounds__(256) ln_param_part_kernel(const __nv_bfloat16*
 constexpr int kLnFoldGroups = 32;
 __global__ void ln_param_grad_kernel(const float* __restrict__ part, int nparts, int H, float* __restrict__ dgamma,
                                      float* __restrict__ dbeta) {
+  pdl_trigger();
+  pdl_wait();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= 2 * H) return;
   const int per = (nparts + gridDim.y - 1) / gridDim.y;
@@ -285,7 +295,7 @@ int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bf
   const int threads = 256;
   const int blocks = (rows * 32 + threads - 1) / threads;
   const int nv = (H / 4 + 31) / 32;
-#define LN_FWD(NVV) ln_fwd_kernel<NVV><<<blocks, threads, 0, s>>>(x, gamma, beta, y, mean, rstd, rows, H, eps)
+#define LN_FWD(NVV) launch_k(ln_fwd_kernel<NVV>, blocks, threads, 0, s, x, gamma, beta, y, mean, rstd, rows, H, eps)
   if (nv <= 2) LN_FWD(2);
   else if (nv <= 6) LN_FWD(6);
   else if (nv <= 8) LN_FWD(8);
@@ -325,7 +335,7 @@ int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, c
   do {                                                                                                   \
     if (smem + kLnStaticSmem > 48 * 1024)                                                                \
       cudaFuncSetAttribute(ln_bwd_kernel<NVV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    ln_bwd_kernel<NVV, true><<<blocks, 256, smem, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16, part, rows, H); \
+    launch_k(ln_bwd_kernel<NVV, true>, blocks, 256, smem, s, dy, x, mean, rstd, gamma, dres, dx, dx_bf16, part, rows, H, AgPush{}); \
   } while (0)
     if (nv <= 2) LN_BWD(2);
     else if (nv <= 6) LN_BWD(6);
@@ -334,17 +344,17 @@ int layernorm_bwd2(const __nv_bfloat16* dy, const float* x, const float* mean, c
   } else {
     const int blocks = std::max(1, (rows * 32 + 255) / 256);
     if (nv <= 16)
-      ln_bwd_kernel<16, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
-                                                                         nullptr, rows, H);
+      launch_k(ln_bwd_kernel<16, false>, std::min(blocks, 1184), 256, 0, s, dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
+                                                                         nullptr, rows, H, AgPush{});
     else
-      ln_bwd_kernel<32, false><<<std::min(blocks, 1184), 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
-                                                                         nullptr, rows, H);
+      launch_k(ln_bwd_kernel<32, false>, std::min(blocks, 1184), 256, 0, s, dy, x, mean, rstd, gamma, dres, dx, dx_bf16,
+                                                                         nullptr, rows, H, AgPush{});
     const int rows_per_band = (rows + nparts - 1) / nparts;
     dim3 grid(nparts, (H + 255) / 256);
-    ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);
+    launch_k(ln_param_part_kernel, grid, 256, 0, s, dy, x, mean, rstd, part, rows, H, rows_per_band);
   }
   dim3 fold((2 * H + 255) / 256, std::min(kLnFoldGroups, nparts));
-  ln_param_grad_kernel<<<fold, 256, 0, s>>>(part, nparts, H, dgamma, dbeta);
+  launch_k(ln_param_grad_kernel, fold, 256, 0, s, part, nparts, H, dgamma, dbeta);
   return (int)cudaGetLastError();
 }
 
@@ -353,7 +363,7 @@ int layernorm_fwd_push(const float* x, const float* gamma, const float* beta, fl
   if (H % 4 != 0 || H > 4096 || push.world < 1 || push.world > 8 || push.Sl <= 0) return -1;
   const int blocks = std::max(1, std::min((rows + 7) / 8, 4 * num_sms));
   const int nv = (H / 4 + 31) / 32;
-#define LN_FWDP(NVV) ln_fwd_push_kernel<NVV><<<blocks, 256, 0, s>>>(x, gamma, beta, mean, rstd, rows, H, eps, push)
+#define LN_FWDP(NVV) launch_k(ln_fwd_push_kernel<NVV>, blocks, 256, 0, s, x, gamma, beta, mean, rstd, rows, H, eps, push)
   if (nv <= 2) LN_FWDP(2);
   else if (nv <= 6) LN_FWDP(6);
   else if (nv <= 8) LN_FWDP(8);
@@ -374,7 +384,7 @@ int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mea
   do {                                                                                                             \
     if (smem + kLnStaticSmem > 48 * 1024)                                                                          \
       cudaFuncSetAttribute(ln_bwd_kernel<NVV, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);     \
-    ln_bwd_kernel<NVV, true, true><<<nparts, 256, smem, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, part, rows, \
+    launch_k(ln_bwd_kernel<NVV, true, true>, nparts, 256, smem, s, dy, x, mean, rstd, gamma, dres, dx, nullptr, part, rows, \
                                                              H, push);                                              \
   } while (0)
     if (nv <= 2) LN_BWDP(2);
@@ -384,17 +394,17 @@ int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mea
   } else {
     const int blocks = std::min(std::max(1, (rows * 32 + 255) / 256), 1184);
     if (nv <= 16)
-      ln_bwd_kernel<16, false, true><<<blocks, 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, nullptr, rows,
+      launch_k(ln_bwd_kernel<16, false, true>, blocks, 256, 0, s, dy, x, mean, rstd, gamma, dres, dx, nullptr, nullptr, rows,
                                                              H, push);
     else
-      ln_bwd_kernel<32, false, true><<<blocks, 256, 0, s>>>(dy, x, mean, rstd, gamma, dres, dx, nullptr, nullptr, rows,
+      launch_k(ln_bwd_kernel<32, false, true>, blocks, 256, 0, s, dy, x, mean, rstd, gamma, dres, dx, nullptr, nullptr, rows,
                                                              H, push);
     const int rows_per_band = (rows + nparts - 1) / nparts;
     dim3 grid(nparts, (H + 255) / 256);
-    ln_param_part_kernel<<<grid, 256, 0, s>>>(dy, x, mean, rstd, part, rows, H, rows_per_band);
+    launch_k(ln_param_part_kernel, grid, 256, 0, s, dy, x, mean, rstd, part, rows, H, rows_per_band);
   }
   dim3 fold((2 * H + 255) / 256, std::min(kLnFoldGroups, nparts));
-  ln_param_grad_kernel<<<fold, 256, 0, s>>>(part, nparts, H, dgamma, dbeta);
+  launch_k(ln_param_grad_kernel, fold, 256, 0, s, part, nparts, H, dgamma, dbeta);
   return (int)cudaGetLastError();
 }
 
