@@ -371,7 +371,7 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
                     const std::vector<int64_t>& pbf16, const std::vector<int64_t>& sig, int64_t rank, int64_t bucket,
                     int64_t epoch, int64_t lo, int64_t hi, Tensor& exp_avg, Tensor& exp_avg_sq, Tensor& counter,
                     double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
-                    int64_t max_ctas) {
+                    int64_t max_ctas, int64_t defer_done) {
   const int world = (int)param.size();
   TORCH_CHECK(world >= 1 && world <= 8 && grad.size() == param.size() && pbf16.size() == param.size() &&
                   sig.size() == param.size(),
@@ -407,6 +407,7 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
   s.counter = reinterpret_cast<unsigned*>(counter.data_ptr<int>());
   s.err = error_word();
   s.max_ctas = (int)max_ctas;
+  s.defer_done = defer_done ? 1 : 0;
   MMB_CHECK_RC(mmb::dp_rs_adamw_ag(P, s, cur_stream()), "dp_rs_adamw_ag");
 }
 
@@ -658,7 +659,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("tensor_from_ptr", &tensor_from_ptr);
-  m.def("dp_rs_adamw_ag", &dp_rs_adamw_ag);
+  m.def("dp_rs_adamw_ag", &dp_rs_adamw_ag, py::arg("param"), py::arg("grad"), py::arg("pbf16"), py::arg("sig"),
+        py::arg("rank"), py::arg("bucket"), py::arg("epoch"), py::arg("lo"), py::arg("hi"), py::arg("exp_avg"),
+        py::arg("exp_avg_sq"), py::arg("counter"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"),
+        py::arg("wd"), py::arg("step"), py::arg("grad_scale"), py::arg("max_ctas"), py::arg("defer_done") = 0);
+  m.def("dp_wait_done", [](int64_t sig_local, int64_t nbuckets, int64_t world, int64_t epoch, int64_t timeout_ms) {
+    MMB_CHECK_RC(mmb::dp_wait_done(reinterpret_cast<const void*>(sig_local), (int)nbuckets, (int)world, (int)epoch,
+                                   (unsigned long long)timeout_ms * 1000000ull, error_word(), cur_stream()),
+                 "dp_wait_done");
+  }, py::arg("sig_local"), py::arg("nbuckets"), py::arg("world"), py::arg("epoch"), py::arg("timeout_ms") = 10000);
   m.def("dp_signal_pad_bytes", &mmb::dp_signal_pad_bytes);
   m.def("layernorm_fwd_push", &layernorm_fwd_push);
   m.def("layernorm_bwd_push", &layernorm_bwd_push);

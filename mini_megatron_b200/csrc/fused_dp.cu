@@ -48,6 +48,7 @@ struct DpArgs {
   float lr, b1, b2, eps, wd, step_size, bc2_sqrt, grad_scale;
   unsigned* counter;    // local CTA-completion counter for this bucket
   int* err;
+  int defer_done;       // 1: publish "done" and return; dp_wait_done_kernel waits for all buckets at step end
 };
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
@@ -143,7 +144,39 @@ __global__ void __launch_bounds__(256) dp_rs_adamw_ag_kernel(const DpPeers P, co
     __threadfence_system();
     st_release_sys(P.sig[threadIdx.x] + slot_done * kDpMaxRanks + a.rank, a.epoch);
   }
+  if (a.defer_done) return;
   wait_flags(P.sig[a.rank], slot_done, world, a.epoch, a.err);
+}
+
+// End of an optimizer step with deferred completion: wait (bounded, polling
+// with a short sleep) until every rank has published "done" for every bucket,
+// i.e. all peers finished reading this rank's gradients and writing its
+// parameters.  One thread per (bucket, rank) flag, strided over the block.
+__global__ void __launch_bounds__(256) dp_wait_done_kernel(const int* __restrict__ pad, int nbuckets, int world,
+                                                           int epoch, unsigned long long timeout_ns, int* err) {
+  pdl_trigger();
+  pdl_wait();
+  const int n = nbuckets * world;
+  const unsigned long long t0 = globaltimer();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int b = i / world, r = i % world;
+    const int* f = pad + (b * 2 + 1) * kDpMaxRanks + r;
+    while (ld_acquire_sys(f) < epoch) {
+      if (globaltimer() - t0 > timeout_ns) {
+        atomicExch(err, kErrPeerWait);
+        return;
+      }
+      __nanosleep(200);
+    }
+  }
+}
+
+int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, unsigned long long timeout_ns, int* err,
+                 cudaStream_t stream) {
+  if (nbuckets < 1 || nbuckets > kDpMaxBuckets || world < 1 || world > kDpMaxRanks) return -1;
+  launch_k(dp_wait_done_kernel, 1, 256, 0, stream, reinterpret_cast<const int*>(sig_local), nbuckets, world, epoch,
+           timeout_ns, err);
+  return (int)cudaGetLastError();
 }
 
 int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t stream) {
@@ -175,6 +208,7 @@ int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t s
   a.grad_scale = s.grad_scale;
   a.counter = s.counter;
   a.err = s.err;
+  a.defer_done = s.defer_done;
   const long n4 = (s.hi - s.lo) / 4;
   const int blocks = (int)std::max<long>(1, std::min<long>((n4 + 255) / 256, s.max_ctas));
   launch_k(dp_rs_adamw_ag_kernel, blocks, 256, 0, stream, P, a);

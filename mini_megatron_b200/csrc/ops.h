@@ -92,8 +92,11 @@ struct DpStepHost {
   unsigned* counter;
   int* err;
   int max_ctas;
+  int defer_done;
 };
 int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t stream);
+int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, unsigned long long timeout_ns, int* err,
+                 cudaStream_t stream);
 int dp_signal_pad_bytes();
 
 }  // namespace mmb

@@ -29,7 +29,7 @@ from .param_buffer import ParamBuffer
 
 class FusedDPOptimizer(torch.optim.Optimizer):
     def __init__(self, module: torch.nn.Module, dp_group, lr=6e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
-                 bucket_elems=16 << 20, overlap=True, max_ctas=64):
+                 bucket_elems=16 << 20, overlap=True, max_ctas=64, defer_done=False, tail_ctas=None):
         C = native()
         self.group = dp_group
         self.world = 1 if dp_group is None else dist.get_world_size(dp_group)
@@ -71,6 +71,13 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         self.overlap = overlap
         self._default_overlap = overlap
         self.max_ctas = max_ctas
+        # defer_done: bucket kernels publish "done" without waiting for the peers; one bounded wait for
+        # every bucket runs at the end of the step (no cross-rank barrier between consecutive buckets).
+        # Buckets launched after backward (nothing left to overlap with) get tail_ctas CTAs.
+        self.defer_done = bool(defer_done)
+        self.tail_ctas = tail_ctas if tail_ctas is not None else (
+            4 * torch.cuda.get_device_properties(self.buf.data.device).multi_processor_count
+            if self.defer_done else max_ctas)
         self._step = 0
         self._epoch = 0
         self._bucket_of = {}
@@ -79,6 +86,7 @@ class FusedDPOptimizer(torch.optim.Optimizer):
                 self._bucket_of[id(p)] = b
         self._pending = []
         self._next = 0
+        self._launched_step = False
         # every rank's buffers hold the same initial values (same seed) -- make the bf16 shadow current
         self.buf.refresh_bf16()
         if self.world > 1:
@@ -121,7 +129,7 @@ class FusedDPOptimizer(torch.optim.Optimizer):
             self._step += 1
             self._epoch += 1
 
-    def _launch(self, b):
+    def _launch(self, b, tail=False):
         self._begin()
         C = native()
         g = self.param_groups[0]
@@ -135,13 +143,16 @@ class FusedDPOptimizer(torch.optim.Optimizer):
             C.dp_rs_adamw_ag(self.ptr_param, self.ptr_grad, self.ptr_bf16, self.ptr_sig, self.rank, b, self._epoch,
                              lo, hi, self.exp_avg[off:off + n], self.exp_avg_sq[off:off + n], self.counters[b:b + 1],
                              g["lr"], g["betas"][0], g["betas"][1], g["eps"], g["weight_decay"], self._step,
-                             1.0 / self.world, self.max_ctas)
+                             1.0 / self.world, self.tail_ctas if tail else self.max_ctas, int(self.defer_done))
 
     def finish(self):
-        """Launch the buckets not yet issued (in order)."""
+        """Launch the buckets not yet issued (in order), then (deferred mode) the wait for every rank's "done"."""
         while self._next < len(self.buf.buckets):
-            self._launch(self._next)
+            self._launch(self._next, tail=True)
             self._next += 1
+        if self.defer_done and self._launched_step:
+            with torch.cuda.stream(self.stream):
+                native().dp_wait_done(self.ptr_sig[self.rank], len(self.buf.buckets), self.world, self._epoch)
 
     # ----------------------------------------------------------- optimizer interface
     @torch.no_grad()

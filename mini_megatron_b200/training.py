@@ -146,9 +146,10 @@ class Trainer:
         self.dp_impl = impl
         if impl == "fused":
             from .parallel.fused_dp import FusedDPOptimizer
+            early = cfg.dp_early_buckets or os.environ.get("MMB_DP_EARLY_BUCKETS") == "1"
             self.optimizer = FusedDPOptimizer(self.model, mpu["dp_group"], lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                               weight_decay=cfg.weight_decay, bucket_elems=bucket_elems,
-                                              overlap=cfg.dp_overlap)
+                                              overlap=cfg.dp_overlap, defer_done=early)
             self.buf = self.optimizer.buf
             self.grad_sync = self.optimizer
         elif cfg.zero1:

@@ -73,9 +73,13 @@ def _train(rank, world, tp, pp, sp, dp_impl, steps, micro, tp_impl="auto"):
 
 
 @NEED2
-def test_fused_dp_matches_nccl_dp():
-    fused = _run(_train, 2, 1, 1, False, "fused", 3, 1, port=29711)
-    nccl = _run(_train, 2, 1, 1, False, "nccl", 3, 1, port=29712)
+@pytest.mark.parametrize("early", [False, True])
+def test_fused_dp_matches_nccl_dp(early):
+    """early: buckets start during backward (head and embedding hooks) and the bucket kernels defer
+    their cross-rank completion wait to one wait at the end of the step."""
+    env = {"MMB_DP_EARLY_BUCKETS": "1"} if early else {}
+    fused = _run(_train, 2, 1, 1, False, "fused", 3, 1, port=29711 + 10 * int(early), env=env)
+    nccl = _run(_train, 2, 1, 1, False, "nccl", 3, 1, port=29712 + 10 * int(early), env=env)
     for r in range(2):
         for k, v in fused[r]["state"].items():
             ref = nccl[r]["state"][k]
