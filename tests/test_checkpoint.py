@@ -115,3 +115,63 @@ def test_corrupt_and_mismatched_checkpoints_fail_cleanly(tmp_path):
     os.remove(tmp_path / "manifest.json")
     with pytest.raises(CheckpointError, match="manifest"):
         load_distributed_checkpoint(str(tmp_path), m, opt, sched)
+
+
+REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+
+
+def _ref_model():
+    import sys
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import config as rcfg
+    from model.embedding import Embedding
+    from model.loss import CrossEntropyLoss
+    from model.transformer import GPT, Decoder
+    from parallel.process_groups import set_model_parallel
+    from parallel.tensor_parallel import ColumnParallelLinear
+    from mini_megatron_b200.config import PRESETS
+    c = PRESETS["tiny"]
+    set_model_parallel(None)
+    torch.manual_seed(1)
+    return GPT(Embedding(c.vocab_size, c.hidden_size, c.max_seq_len),
+               Decoder(c.hidden_size, c.num_attention_heads, c.ffn_hidden_size, c.num_layers),
+               torch.nn.LayerNorm(c.hidden_size),
+               ColumnParallelLinear(c.hidden_size, c.vocab_size, bias=False, gather_output=True), CrossEntropyLoss())
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REF, "checkpoint.py")), reason="reference sources not present")
+@pytest.mark.parametrize("direction", ["reference_to_ours", "ours_to_reference"])
+def test_checkpoints_interchange_with_the_reference(tmp_path, direction):
+    """A checkpoint written by the reference's checkpoint.py loads here (model, optimizer, scheduler, step)
+    and continues training identically, and vice versa."""
+    import importlib.util
+    import sys
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    spec = importlib.util.spec_from_file_location("ref_checkpoint", os.path.join(REF, "checkpoint.py"))
+    ref_ck = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref_ck)
+    from mini_megatron_b200.utils import checkpoint as our_ck
+    src_model = _ref_model() if direction == "reference_to_ours" else _tiny()
+    dst_model = _tiny() if direction == "reference_to_ours" else _ref_model()
+    mk = lambda m: torch.optim.AdamW(m.parameters(), lr=1e-3, weight_decay=0.1)  # noqa: E731
+    src_opt, dst_opt = mk(src_model), mk(dst_model)
+    src_sched = torch.optim.lr_scheduler.LambdaLR(src_opt, lambda s: min(1.0, (s + 1) / 10))
+    dst_sched = torch.optim.lr_scheduler.LambdaLR(dst_opt, lambda s: min(1.0, (s + 1) / 10))
+    torch.manual_seed(5)
+    _train_one(src_model, src_opt, src_sched)
+    path = str(tmp_path / "ck.pt")
+    save = ref_ck.save_checkpoint if direction == "reference_to_ours" else our_ck.save_checkpoint
+    load = our_ck.load_checkpoint if direction == "reference_to_ours" else ref_ck.load_checkpoint
+    save(src_model, src_opt, src_sched, 3, path)
+    assert load(dst_model, dst_opt, dst_sched, path, "cpu") == 3
+    for (na, a), (nb, b) in zip(src_model.state_dict().items(), dst_model.state_dict().items()):
+        assert na == nb and torch.equal(a, b)
+    # one more identical step on both keeps them identical (optimizer state and LR came across)
+    torch.manual_seed(9)
+    _train_one(src_model, src_opt, src_sched)
+    torch.manual_seed(9)
+    _train_one(dst_model, dst_opt, dst_sched)
+    for a, b in zip(src_model.state_dict().values(), dst_model.state_dict().values()):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
