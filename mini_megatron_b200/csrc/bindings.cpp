@@ -371,7 +371,8 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
                     const std::vector<int64_t>& pbf16, const std::vector<int64_t>& sig, int64_t rank, int64_t bucket,
                     int64_t epoch, int64_t lo, int64_t hi, Tensor& exp_avg, Tensor& exp_avg_sq, Tensor& counter,
                     double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
-                    int64_t max_ctas, int64_t defer_done) {
+                    int64_t max_ctas, int64_t defer_done, const c10::optional<Tensor>& epoch_dev,
+                    const c10::optional<Tensor>& hyper) {
   const int world = (int)param.size();
   TORCH_CHECK(world >= 1 && world <= 8 && grad.size() == param.size() && pbf16.size() == param.size() &&
                   sig.size() == param.size(),
@@ -408,6 +409,14 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
   s.err = error_word();
   s.max_ctas = (int)max_ctas;
   s.defer_done = defer_done ? 1 : 0;
+  if (epoch_dev.has_value()) {
+    TORCH_CHECK(epoch_dev->scalar_type() == at::kInt && epoch_dev->is_cuda(), "epoch_dev must be a CUDA int32");
+    s.epoch_ptr = epoch_dev->data_ptr<int>();
+  }
+  if (hyper.has_value()) {
+    check_f32(*hyper, "hyper");
+    s.hyper = hyper->data_ptr<float>();
+  }
   MMB_CHECK_RC(mmb::dp_rs_adamw_ag(P, s, cur_stream()), "dp_rs_adamw_ag");
 }
 
@@ -662,12 +671,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_rs_adamw_ag", &dp_rs_adamw_ag, py::arg("param"), py::arg("grad"), py::arg("pbf16"), py::arg("sig"),
         py::arg("rank"), py::arg("bucket"), py::arg("epoch"), py::arg("lo"), py::arg("hi"), py::arg("exp_avg"),
         py::arg("exp_avg_sq"), py::arg("counter"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"),
-        py::arg("wd"), py::arg("step"), py::arg("grad_scale"), py::arg("max_ctas"), py::arg("defer_done") = 0);
-  m.def("dp_wait_done", [](int64_t sig_local, int64_t nbuckets, int64_t world, int64_t epoch, int64_t timeout_ms) {
+        py::arg("wd"), py::arg("step"), py::arg("grad_scale"), py::arg("max_ctas"), py::arg("defer_done") = 0,
+        py::arg("epoch_dev") = c10::nullopt, py::arg("hyper") = c10::nullopt);
+  m.def("dp_wait_done", [](int64_t sig_local, int64_t nbuckets, int64_t world, int64_t epoch,
+                           const c10::optional<Tensor>& epoch_dev, int64_t timeout_ms) {
+    const int* ep = epoch_dev.has_value() ? epoch_dev->data_ptr<int>() : nullptr;
     MMB_CHECK_RC(mmb::dp_wait_done(reinterpret_cast<const void*>(sig_local), (int)nbuckets, (int)world, (int)epoch,
-                                   (unsigned long long)timeout_ms * 1000000ull, error_word(), cur_stream()),
+                                   ep, (unsigned long long)timeout_ms * 1000000ull, error_word(), cur_stream()),
                  "dp_wait_done");
-  }, py::arg("sig_local"), py::arg("nbuckets"), py::arg("world"), py::arg("epoch"), py::arg("timeout_ms") = 10000);
+  }, py::arg("sig_local"), py::arg("nbuckets"), py::arg("world"), py::arg("epoch"),
+        py::arg("epoch_dev") = c10::nullopt, py::arg("timeout_ms") = 10000);
+  m.def("dp_epoch_step", [](Tensor& epoch) {
+    TORCH_CHECK(epoch.scalar_type() == at::kInt && epoch.is_cuda() && epoch.numel() == 1, "epoch: one CUDA int32");
+    MMB_CHECK_RC(mmb::dp_epoch_step(epoch.data_ptr<int>(), cur_stream()), "dp_epoch_step");
+  });
   m.def("dp_signal_pad_bytes", &mmb::dp_signal_pad_bytes);
   m.def("layernorm_fwd_push", &layernorm_fwd_push);
   m.def("layernorm_bwd_push", &layernorm_bwd_push);

@@ -49,6 +49,8 @@ struct DpArgs {
   unsigned* counter;    // local CTA-completion counter for this bucket
   int* err;
   int defer_done;       // 1: publish "done" and return; dp_wait_done_kernel waits for all buckets at step end
+  const int* epoch_ptr;   // non-null: the epoch is read from device memory (CUDA-graph replays)
+  const float* hyper;     // non-null: {lr, lr / bc1, sqrt(bc2)} from device memory (see adamw_hyper_step)
 };
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
@@ -77,9 +79,15 @@ __device__ bool wait_flags(const int* pad, int slot, int world, int epoch, int* 
   return __syncthreads_and(ok) != 0;
 }
 
-__global__ void __launch_bounds__(256) dp_rs_adamw_ag_kernel(const DpPeers P, const DpArgs a) {
+__global__ void __launch_bounds__(256) dp_rs_adamw_ag_kernel(const DpPeers P, DpArgs a) {
   pdl_trigger();
   pdl_wait();
+  if (a.epoch_ptr) a.epoch = *a.epoch_ptr;
+  if (a.hyper) {
+    a.lr = a.hyper[0];
+    a.step_size = a.hyper[1];
+    a.bc2_sqrt = a.hyper[2];
+  }
   const int world = a.world;
   const int slot_ready = a.bucket * 2, slot_done = a.bucket * 2 + 1;
   // 1. publish "my gradients of this bucket are final" (written by earlier kernels on this stream)
@@ -153,9 +161,11 @@ __global__ void __launch_bounds__(256) dp_rs_adamw_ag_kernel(const DpPeers P, co
 // i.e. all peers finished reading this rank's gradients and writing its
 // parameters.  One thread per (bucket, rank) flag, strided over the block.
 __global__ void __launch_bounds__(256) dp_wait_done_kernel(const int* __restrict__ pad, int nbuckets, int world,
-                                                           int epoch, unsigned long long timeout_ns, int* err) {
+                                                           int epoch, const int* __restrict__ epoch_ptr,
+                                                           unsigned long long timeout_ns, int* err) {
   pdl_trigger();
   pdl_wait();
+  if (epoch_ptr) epoch = *epoch_ptr;
   const int n = nbuckets * world;
   const unsigned long long t0 = globaltimer();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -171,11 +181,23 @@ __global__ void __launch_bounds__(256) dp_wait_done_kernel(const int* __restrict
   }
 }
 
-int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, unsigned long long timeout_ns, int* err,
-                 cudaStream_t stream) {
+int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, const int* epoch_ptr,
+                 unsigned long long timeout_ns, int* err, cudaStream_t stream) {
   if (nbuckets < 1 || nbuckets > kDpMaxBuckets || world < 1 || world > kDpMaxRanks) return -1;
   launch_k(dp_wait_done_kernel, 1, 256, 0, stream, reinterpret_cast<const int*>(sig_local), nbuckets, world, epoch,
-           timeout_ns, err);
+           epoch_ptr, timeout_ns, err);
+  return (int)cudaGetLastError();
+}
+
+// One thread: advance the device epoch of the cross-rank flags by one step.
+__global__ void dp_epoch_step_kernel(int* __restrict__ epoch) {
+  pdl_trigger();
+  pdl_wait();
+  if (blockIdx.x == 0 && threadIdx.x == 0) *epoch += 1;
+}
+
+int dp_epoch_step(int* epoch, cudaStream_t stream) {
+  launch_k(dp_epoch_step_kernel, 1, 32, 0, stream, epoch);
   return (int)cudaGetLastError();
 }
 
@@ -209,6 +231,8 @@ int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t s
   a.counter = s.counter;
   a.err = s.err;
   a.defer_done = s.defer_done;
+  a.epoch_ptr = s.epoch_ptr;
+  a.hyper = s.hyper;
   const long n4 = (s.hi - s.lo) / 4;
   const int blocks = (int)std::max<long>(1, std::min<long>((n4 + 255) / 256, s.max_ctas));
   launch_k(dp_rs_adamw_ag_kernel, blocks, 256, 0, stream, P, a);

@@ -93,10 +93,13 @@ struct DpStepHost {
   int* err;
   int max_ctas;
   int defer_done;
+  const int* epoch_ptr;
+  const float* hyper;
 };
 int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t stream);
-int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, unsigned long long timeout_ns, int* err,
-                 cudaStream_t stream);
+int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, const int* epoch_ptr,
+                 unsigned long long timeout_ns, int* err, cudaStream_t stream);
+int dp_epoch_step(int* epoch, cudaStream_t stream);
 int dp_signal_pad_bytes();
 
 }  // namespace mmb

@@ -60,6 +60,10 @@ class FusedAdamW(torch.optim.Optimizer):
         self._dev_hyper = torch.zeros(4, dtype=torch.float32, device=dev)
         self._lr_table = lr_table.to(device=dev, dtype=torch.float32).contiguous()
 
+    def advance_host_counters(self):
+        """Host-side bookkeeping of one replayed step (the replay itself advances the device counter)."""
+        self._step += 1
+
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None

@@ -87,6 +87,7 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         self._pending = []
         self._next = 0
         self._launched_step = False
+        self._dev_epoch = self._dev_step = self._dev_hyper = self._lr_table = None
         # every rank's buffers hold the same initial values (same seed) -- make the bf16 shadow current
         self.buf.refresh_bf16()
         if self.world > 1:
@@ -129,7 +130,26 @@ class FusedDPOptimizer(torch.optim.Optimizer):
             self._step += 1
             self._epoch += 1
 
+    def enable_device_schedule(self, lr_table: torch.Tensor):
+        """Keep the flag epoch, the step count and lr on the device, so a captured step replays correctly.
+
+        At the first bucket of each step a one-thread kernel advances the epoch
+        and another derives lr and the bias corrections from the step counter
+        (``lr_table[step - 1]``); the bucket kernels read them from memory.
+        """
+        dev = self.buf.data.device
+        self._dev_epoch = torch.tensor([self._epoch], dtype=torch.int32, device=dev)
+        self._dev_step = torch.tensor([self._step], dtype=torch.int32, device=dev)
+        self._dev_hyper = torch.zeros(4, dtype=torch.float32, device=dev)
+        self._lr_table = lr_table.to(device=dev, dtype=torch.float32).contiguous()
+
+    def advance_host_counters(self):
+        """Host-side bookkeeping of one replayed step (the replay itself advances the device counters)."""
+        self._step += 1
+        self._epoch += 1
+
     def _launch(self, b, tail=False):
+        first = not self._launched_step
         self._begin()
         C = native()
         g = self.param_groups[0]
@@ -140,10 +160,14 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         ev.record(torch.cuda.current_stream())
         self.stream.wait_event(ev)
         with torch.cuda.stream(self.stream):
+            if first and self._dev_epoch is not None:
+                C.dp_epoch_step(self._dev_epoch)
+                C.adamw_hyper_step(self._dev_step, self._lr_table, g["betas"][0], g["betas"][1], self._dev_hyper)
             C.dp_rs_adamw_ag(self.ptr_param, self.ptr_grad, self.ptr_bf16, self.ptr_sig, self.rank, b, self._epoch,
                              lo, hi, self.exp_avg[off:off + n], self.exp_avg_sq[off:off + n], self.counters[b:b + 1],
                              g["lr"], g["betas"][0], g["betas"][1], g["eps"], g["weight_decay"], self._step,
-                             1.0 / self.world, self.tail_ctas if tail else self.max_ctas, int(self.defer_done))
+                             1.0 / self.world, self.tail_ctas if tail else self.max_ctas, int(self.defer_done),
+                             self._dev_epoch, self._dev_hyper)
 
     def finish(self):
         """Launch the buckets not yet issued (in order), then (deferred mode) the wait for every rank's "done"."""
@@ -152,7 +176,8 @@ class FusedDPOptimizer(torch.optim.Optimizer):
             self._next += 1
         if self.defer_done and self._launched_step:
             with torch.cuda.stream(self.stream):
-                native().dp_wait_done(self.ptr_sig[self.rank], len(self.buf.buckets), self.world, self._epoch)
+                native().dp_wait_done(self.ptr_sig[self.rank], len(self.buf.buckets), self.world, self._epoch,
+                                      self._dev_epoch)
 
     # ----------------------------------------------------------- optimizer interface
     @torch.no_grad()
@@ -175,6 +200,10 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         if sd["dp_size"] != self.world or list(map(tuple, sd["shards"])) != list(map(tuple, self.shards)):
             raise ValueError("fused-DP state was saved with a different DP layout")
         self._step = int(sd["step"])
+        self._epoch = int(sd.get("epoch", self._epoch))
+        if self._dev_step is not None:
+            self._dev_step.fill_(self._step)
+            self._dev_epoch.fill_(self._epoch)
         self.exp_avg.copy_(sd["exp_avg"])
         self.exp_avg_sq.copy_(sd["exp_avg_sq"])
         for g, s in zip(self.param_groups, sd["param_groups"]):

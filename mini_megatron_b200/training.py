@@ -229,10 +229,14 @@ class Trainer:
         the flat fused AdamW; other layouts run eagerly.
         """
         cfg = self.cfg
-        supported = (self.device.type == "cuda" and cfg.tp == 1 and cfg.pp == 1 and self.mpu["dp_size"] == 1
-                     and isinstance(self.optimizer, FusedAdamW) and not self.optimizer._loose)
+        single = (self.mpu["dp_size"] == 1 and isinstance(self.optimizer, FusedAdamW) and not self.optimizer._loose)
+        # the fused-DP step (no NCCL inside) with device-side epochs; gated with the early-bucket mode
+        fused_dp = (self.dp_impl == "fused" and self.mpu["dp_size"] > 1 and not self.mpu["sequence_parallel"]
+                    and (cfg.dp_early_buckets or os.environ.get("MMB_DP_EARLY_BUCKETS") == "1"))
+        supported = self.device.type == "cuda" and cfg.tp == 1 and cfg.pp == 1 and (single or fused_dp)
         if cfg.cuda_graph == "on" and not supported:
-            raise ValueError("cuda_graph='on' needs CUDA, tp = pp = dp = 1 and the flat fused AdamW")
+            raise ValueError("cuda_graph='on' needs CUDA, tp = pp = 1 and either dp = 1 with the flat fused AdamW "
+                             "or the fused-DP optimizer in early-bucket mode")
         self.graph_mode = supported and cfg.cuda_graph in ("on", "auto") and os.environ.get("MMB_CUDA_GRAPH") != "0"
         self._graph = None
         self._graph_calls = 0
@@ -289,7 +293,7 @@ class Trainer:
             self._graph = g
             # capturing ran this step's host-side bookkeeping (scheduler, step counters) once; now run its kernels
         else:
-            self.optimizer._step += 1
+            self.optimizer.advance_host_counters()
             self.scheduler.step()
             self.step_count += 1
         self._graph.replay()
