@@ -325,3 +325,43 @@ def test_loss_parsing_and_curve_record():
     assert legacy.parse_report(out) == {"throughput": 1000.0, "mfu": 1.5}
     rec = legacy.loss_curve_record("t", "m", "d", {}, {"ours": [(1, 6.9)]}, "c")
     assert rec["results"]["ours"] == [{"step": 1, "loss": 6.9}]
+
+
+# ----------------------------------------------------------------------------- command lines
+def test_command_lines_end_to_end(tmp_path, capsys, monkeypatch):
+    """The harness modules' CLIs: bundle run/validate, paired summary, campaign init/record/validate,
+    kernel classification, artifacts, legacy datasets and conclusions."""
+    from mini_megatron_b200.harness import artifacts as A
+    # no nvidia-smi here: record the preflight of an idle GPU host so the bundles qualify for pairing
+    monkeypatch.setattr(B, "gpu_preflight", lambda: {"command": ["nvidia-smi"], "return_code": 0, "stdout": "",
+                                                      "stderr": "", "active_processes": []})
+    from mini_megatron_b200.harness import kernels as KN
+    results = tmp_path / "runs"
+    cmd = [sys.executable, "-c", "print('Throughput:      2,000 tok/s')"]
+    for pair, order in (("01", ("ours", "reference")), ("02", ("reference", "ours"))):
+        for v in order:
+            rc = B.main(["run", "--name", f"p{pair}-{v}", "--results-dir", str(results), "--tag", f"variant={v}",
+                         "--tag", f"pair={pair}", "--tag", "condition=c", "--allow-dirty", "--allow-active-gpus",
+                         "--"] + cmd)
+            assert rc == 0
+    bundles = sorted(results.iterdir())
+    assert len(bundles) == 4 and B.main(["validate", str(bundles[0])]) == 0
+    capsys.readouterr()
+    out = tmp_path / "paired.json"
+    assert paired.main(["--results-dir", str(results), "--min-pairs", "2", "--allow-dirty", "--output",
+                        str(out)]) == 0
+    rep = json.loads(out.read_text())
+    assert rep["paired_ratio_left_over_right"]["mean"] == 1.0
+    camp = tmp_path / "camp"
+    assert campaign.main(["init", "--campaign-dir", str(camp), "--campaign-id", "t"]) == 0
+    assert campaign.main(["record", "--campaign-dir", str(camp), "--kind", "benchmark_summary", "--topology",
+                          "tp1-pp1-dp1", "--source", str(out)]) == 0
+    assert campaign.main(["validate", "--campaign-dir", str(camp)]) == 0
+    rows = tmp_path / "rows.json"
+    rows.write_text(json.dumps([{"name": "mmb::adamw_kernel", "total_time_ns": 5, "instances": 1}]))
+    assert KN.main([str(rows)]) == 0
+    assert A.main(["--output-dir", str(tmp_path / "art"), "--preset", "tiny", "--batches", "2", "--batch-size",
+                   "1"]) == 0
+    assert legacy.main(["synthetic", str(tmp_path / "syn.pt"), "--num-steps", "2", "--batch-size", "1",
+                        "--seq-len", "8"]) == 0
+    assert legacy.main(["identity", str(tmp_path / "syn.pt"), str(tmp_path / "id.pt")]) == 0
