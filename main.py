@@ -60,6 +60,8 @@ def parse_args(argv=None):
     p.add_argument("--ffn-hidden-size", type=int)
     p.add_argument("--vocab-size", type=int)
     p.add_argument("--seq-len", type=int)
+    p.add_argument("--vocab-pad", type=int, default=None,
+                   help="pad the vocabulary tables to a multiple of this times tp (default 128)")
     p.add_argument("--num-microbatches", type=int, default=1)
     p.add_argument("--sequence-parallel", action="store_true")
     p.add_argument("--zero1", action="store_true")
@@ -91,6 +93,10 @@ def model_config(args) -> GPTConfig:
             setattr(base, f, v)
     if args.seq_len is not None:
         base.max_seq_len = max(base.max_seq_len, args.seq_len)
+    if args.vocab_pad is not None:
+        if args.vocab_pad < 1:
+            raise SystemExit("--vocab-pad must be positive")
+        base.vocab_pad_multiple = args.vocab_pad
     return base
 
 
