@@ -186,7 +186,7 @@ def main(argv=None):
                                                       if device.type == "cuda" else 0.0)})
     if args.save:
         save_distributed_checkpoint(args.save, *trainer.state_for_checkpoint(), start_step + steps, mpu=mpu,
-                                    sharded_optimizer=args.zero1)
+                                    sharded_optimizer=args.zero1 or trainer.dp_impl == "fused")
     if is_reporter:
         B = args.micro_batch_size
         per_replica = B * S * m * steps / elapsed

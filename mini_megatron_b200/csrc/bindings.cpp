@@ -47,6 +47,13 @@ int64_t get_error() {
 
 void clear_error() { C10_CUDA_CHECK(cudaMemset(error_word(), 0, sizeof(int))); }
 
+// Host-side write of the error word: lets tests check that the host notices a
+// recorded kernel error without making any kernel time out.
+void set_error(int64_t code) {
+  const int h = (int)code;
+  C10_CUDA_CHECK(cudaMemcpy(error_word(), &h, sizeof(int), cudaMemcpyHostToDevice));
+}
+
 // ----------------------------------------------------------------- GEMM
 void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, Tensor& D, int64_t epi,
           const c10::optional<Tensor>& aux, const c10::optional<Tensor>& resid, double alpha, int64_t bn) {
@@ -372,7 +379,7 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
                     int64_t epoch, int64_t lo, int64_t hi, Tensor& exp_avg, Tensor& exp_avg_sq, Tensor& counter,
                     double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
                     int64_t max_ctas, int64_t defer_done, const c10::optional<Tensor>& epoch_dev,
-                    const c10::optional<Tensor>& hyper) {
+                    const c10::optional<Tensor>& hyper, const c10::optional<Tensor>& segs) {
   const int world = (int)param.size();
   TORCH_CHECK(world >= 1 && world <= 8 && grad.size() == param.size() && pbf16.size() == param.size() &&
                   sig.size() == param.size(),
@@ -417,7 +424,24 @@ void dp_rs_adamw_ag(const std::vector<int64_t>& param, const std::vector<int64_t
     check_f32(*hyper, "hyper");
     s.hyper = hyper->data_ptr<float>();
   }
+  if (segs.has_value()) {
+    TORCH_CHECK(segs->is_cuda() && segs->scalar_type() == at::kInt && segs->dim() == 2 && segs->size(1) == 4 &&
+                    segs->is_contiguous(),
+                "segs: contiguous CUDA int32 [nseg, 4]");
+    s.segs = segs->data_ptr<int>();
+    s.nseg = (int)segs->size(0);
+  }
   MMB_CHECK_RC(mmb::dp_rs_adamw_ag(P, s, cur_stream()), "dp_rs_adamw_ag");
+}
+
+void dp_gather_master(const std::vector<int64_t>& param, int64_t rank, int64_t start, int64_t end) {
+  const int world = (int)param.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world, "fused DP needs 1..8 ranks");
+  mmb::DpPeersHost P{};
+  P.world = world;
+  P.rank = (int)rank;
+  for (int r = 0; r < world; ++r) P.param[r] = reinterpret_cast<void*>(param[r]);
+  MMB_CHECK_RC(mmb::dp_gather_master(P, start, end, num_sms(), cur_stream()), "dp_gather_master");
 }
 
 // ----------------------------------------------------------------- fused tensor parallel
@@ -645,6 +669,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("install_crash_handler", &install_crash_handler,
         "print a native backtrace on SIGSEGV/SIGBUS before the previous handler runs");
   m.def("clear_error", &clear_error);
+  m.def("set_error", &set_error, "write the device error word from the host (tests of the host-side check)");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("D"), py::arg("epi"), py::arg("aux") = c10::nullopt,
         py::arg("resid") = c10::nullopt, py::arg("alpha") = 1.0, py::arg("bn") = 0);
@@ -672,7 +697,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank"), py::arg("bucket"), py::arg("epoch"), py::arg("lo"), py::arg("hi"), py::arg("exp_avg"),
         py::arg("exp_avg_sq"), py::arg("counter"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"),
         py::arg("wd"), py::arg("step"), py::arg("grad_scale"), py::arg("max_ctas"), py::arg("defer_done") = 0,
-        py::arg("epoch_dev") = c10::nullopt, py::arg("hyper") = c10::nullopt);
+        py::arg("epoch_dev") = c10::nullopt, py::arg("hyper") = c10::nullopt, py::arg("segs") = c10::nullopt);
+  m.def("dp_gather_master", &dp_gather_master, "copy the other ranks' fp32 master shards of one bucket here",
+        py::arg("param"), py::arg("rank"), py::arg("start"), py::arg("end"));
   m.def("dp_wait_done", [](int64_t sig_local, int64_t nbuckets, int64_t world, int64_t epoch,
                            const c10::optional<Tensor>& epoch_dev, int64_t timeout_ms) {
     const int* ep = epoch_dev.has_value() ? epoch_dev->data_ptr<int>() : nullptr;
@@ -686,6 +713,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     MMB_CHECK_RC(mmb::dp_epoch_step(epoch.data_ptr<int>(), cur_stream()), "dp_epoch_step");
   });
   m.def("dp_signal_pad_bytes", &mmb::dp_signal_pad_bytes);
+  m.def("dp_max_segments", &mmb::dp_max_segments);
   m.def("layernorm_fwd_push", &layernorm_fwd_push);
   m.def("layernorm_bwd_push", &layernorm_bwd_push);
   m.def("tp_ag_push", &tp_ag_push);

@@ -95,8 +95,12 @@ struct DpStepHost {
   int defer_done;
   const int* epoch_ptr;
   const float* hyper;
+  const void* segs;  // int32 [nseg][4]: {begin4, end4, kind, 0} runs of the owned range (nullptr: all kind 2)
+  int nseg;
 };
 int dp_rs_adamw_ag(const DpPeersHost& peers, const DpStepHost& s, cudaStream_t stream);
+int dp_gather_master(const DpPeersHost& peers, long start, long end, int num_sms, cudaStream_t stream);
+int dp_max_segments();
 int dp_wait_done(const void* sig_local, int nbuckets, int world, int epoch, const int* epoch_ptr,
                  unsigned long long timeout_ns, int* err, cudaStream_t stream);
 int dp_epoch_step(int* epoch, cudaStream_t stream);

@@ -58,11 +58,15 @@ def _now():
 
 
 def _write_new(path, obj):
+    """Create ``path`` holding ``obj`` as JSON; ledger entries are write-once, so an existing file is an error."""
     path = Path(path)
-    if path.exists():
-        raise ValueError(f"refusing to overwrite immutable evidence: {path}")
     path.parent.mkdir(parents=True, exist_ok=True)
-    path.write_text(json.dumps(obj, indent=2, sort_keys=True) + "\n", encoding="utf-8")
+    try:
+        with open(path, "x", encoding="utf-8") as f:   # exclusive create: never replaces an entry
+            json.dump(obj, f, indent=2, sort_keys=True)
+            f.write("\n")
+    except FileExistsError:
+        raise ValueError(f"ledger entry {path} already exists; entries are never rewritten") from None
 
 
 def load(campaign_dir) -> dict:

@@ -34,16 +34,22 @@ from .contract import CONTRACT
 
 
 def _init(device_type):
+    kw = {}
     if "RANK" not in os.environ:
-        os.environ.update(RANK="0", LOCAL_RANK="0", WORLD_SIZE="1", MASTER_ADDR="127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", str(29300 + os.getpid() % 500))
+        # a lone process: rendezvous through a private file instead of a TCP port that may be taken
+        import tempfile
+        os.environ.update(RANK="0", LOCAL_RANK="0", WORLD_SIZE="1")
+        fd, path = tempfile.mkstemp(prefix="mmb_fair_bench_rdzv_")
+        os.close(fd)
+        os.unlink(path)
+        kw = dict(init_method=f"file://{path}", rank=0, world_size=1)
     local = int(os.environ["LOCAL_RANK"])
     if device_type == "cuda":
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+                                device_id=torch.device("cuda", local), **kw)
         return torch.device("cuda", local)
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300), **kw)
     return torch.device("cpu")
 
 

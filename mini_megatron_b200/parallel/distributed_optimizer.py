@@ -44,6 +44,11 @@ class DistributedOptimizer(torch.optim.Optimizer):
         self.exp_avg_sq = torch.zeros_like(self.exp_avg)
         self._step = 0
 
+    @property
+    def state_is_sharded(self):
+        """Each DP rank holds only its own slice of the moments (checkpoints write one file per DP rank)."""
+        return self.dp_size > 1
+
     @torch.no_grad()
     def step(self, closure=None):
         loss = closure() if closure is not None else None

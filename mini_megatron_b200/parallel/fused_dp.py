@@ -5,10 +5,17 @@ soon as backward has finished every parameter of that bucket:
 
     peer loads of the owned 1/dp slice of every rank's gradient (NVLink)
     -> sum, scale by 1/dp -> fp32 AdamW with this rank's sharded moments
-    -> peer stores of the new fp32 parameters and bf16 shadows into every rank
+    -> peer stores into every rank of the copy the forward kernels read:
+       the bf16 shadow of a GEMM weight, the fp32 value of a LayerNorm or
+       embedding parameter
 
 so the data-parallel communication and the whole optimizer step overlap the
 rest of backward, and no rank holds more than 1/dp of the optimizer state.
+The fp32 master of a GEMM weight is current only on the rank that owns its
+shard (ZeRO-1): :meth:`FusedDPOptimizer.gather_master` copies the other
+shards in with peer loads, and runs automatically before the model's
+``state_dict()``.  Code that reads GEMM-weight parameters directly between
+steps (rather than through ``state_dict``) calls it first.
 The parameter, gradient and bf16 buffers of the model chunk live in one
 symmetric (peer-mapped) allocation together with a signal pad used for the
 cross-rank ready/done flags.  All ranks of the DP group must share a node.
@@ -67,6 +74,10 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         self.exp_avg = torch.zeros(off, dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros(off, dtype=torch.float32, device=dev)
         self.counters = torch.zeros(len(self.buf.buckets), dtype=torch.int32, device=dev)
+        self.segs = self._replication_runs(module)
+        self._master_stale = False
+        # state_dict() must see the current fp32 master of every shard
+        self._sd_hook = module.register_state_dict_pre_hook(lambda *args, **kw: self.gather_master())
         self.stream = torch.cuda.Stream(device=dev)
         self.overlap = overlap
         self._default_overlap = overlap
@@ -76,8 +87,7 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         # Buckets launched after backward (nothing left to overlap with) get tail_ctas CTAs.
         self.defer_done = bool(defer_done)
         self.tail_ctas = tail_ctas if tail_ctas is not None else (
-            4 * torch.cuda.get_device_properties(self.buf.data.device).multi_processor_count
-            if self.defer_done else max_ctas)
+            4 * torch.cuda.get_device_properties(self.buf.data.device).multi_processor_count)
         self._step = 0
         self._epoch = 0
         self._bucket_of = {}
@@ -92,6 +102,60 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         self.buf.refresh_bf16()
         if self.world > 1:
             dist.barrier(group=dp_group)
+
+    def _replication_runs(self, module):
+        """Per bucket: int32 [nseg, 4] runs {begin4, end4, kind, 0} of this rank's owned range.
+
+        kind 0: a GEMM weight -- the kernels read its bf16 shadow, so only that is all-gathered;
+        kind 1: LayerNorm / embedding parameters and 1-D tensors -- their kernels read fp32.
+        Padding after a parameter belongs to that parameter's run.  A bucket with more runs than
+        the kernel stages gets None (every element is then all-gathered in both precisions).
+        """
+        from .tensor_parallel import VocabParallelEmbedding
+        fp32_ids = set()
+        for m in module.modules():
+            if isinstance(m, (torch.nn.LayerNorm, torch.nn.Embedding, VocabParallelEmbedding)):
+                fp32_ids.update(id(p) for p in m.parameters(recurse=False))
+        kind_of = {id(p): (1 if (id(p) in fp32_ids or p.dim() != 2) else 0) for p in self.buf.params}
+        starts = [(off, kind_of[id(p)]) for p, off in zip(self.buf.params, self.buf.offsets)]
+        max_segs = native().dp_max_segments()
+        out = []
+        for b, (lo, hi) in enumerate(self.shards):
+            runs = []
+            for i, (off, kind) in enumerate(starts):
+                end = starts[i + 1][0] if i + 1 < len(starts) else self.buf.numel
+                a, z = max(off, lo), min(end, hi)
+                if a >= z:
+                    continue
+                if runs and runs[-1][2] == kind and runs[-1][1] == (a - lo) // 4:
+                    runs[-1][1] = (z - lo) // 4
+                else:
+                    runs.append([(a - lo) // 4, (z - lo) // 4, kind, 0])
+            if not runs or len(runs) > max_segs:
+                out.append(None)
+            else:
+                out.append(torch.tensor(runs, dtype=torch.int32).to(self.buf.data.device))
+        return out
+
+    @torch.no_grad()
+    def gather_master(self):
+        """Make this rank's fp32 master current everywhere (peer loads of the owners' shards).
+
+        Stream-ordered after the last step on this rank; the owners cannot
+        update their shards again before this rank starts its next step.
+        """
+        if self.world == 1 or not self._master_stale:
+            return
+        torch.cuda.current_stream().wait_stream(self.stream)
+        C = native()
+        for (lo, hi, _) in self.buf.buckets:
+            C.dp_gather_master(self.ptr_param, self.rank, lo, hi)
+        self._master_stale = False
+
+    @property
+    def state_is_sharded(self):
+        """Each DP rank holds only its own slice of the moments (checkpoints write one file per DP rank)."""
+        return self.world > 1
 
     # ----------------------------------------------------------- GradSync interface
     @property
@@ -147,6 +211,7 @@ class FusedDPOptimizer(torch.optim.Optimizer):
         """Host-side bookkeeping of one replayed step (the replay itself advances the device counters)."""
         self._step += 1
         self._epoch += 1
+        self._master_stale = True
 
     def _launch(self, b, tail=False):
         first = not self._launched_step
@@ -167,7 +232,8 @@ class FusedDPOptimizer(torch.optim.Optimizer):
                              lo, hi, self.exp_avg[off:off + n], self.exp_avg_sq[off:off + n], self.counters[b:b + 1],
                              g["lr"], g["betas"][0], g["betas"][1], g["eps"], g["weight_decay"], self._step,
                              1.0 / self.world, self.tail_ctas if tail else self.max_ctas, int(self.defer_done),
-                             self._dev_epoch, self._dev_hyper)
+                             self._dev_epoch, self._dev_hyper, self.segs[b])
+        self._master_stale = True
 
     def finish(self):
         """Launch the buckets not yet issued (in order), then (deferred mode) the wait for every rank's "done"."""
@@ -206,11 +272,16 @@ class FusedDPOptimizer(torch.optim.Optimizer):
             self._dev_epoch.fill_(self._epoch)
         self.exp_avg.copy_(sd["exp_avg"])
         self.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        # a model state loaded with it holds the full fp32 master on every rank
+        self._master_stale = False
         for g, s in zip(self.param_groups, sd["param_groups"]):
             g.update(s)
         self.buf.refresh_bf16()
 
     def close(self):
+        if getattr(self, "_sd_hook", None) is not None:
+            self._sd_hook.remove()
+            self._sd_hook = None
         if self.symm is not None:
             torch.cuda.synchronize()
             if self.world > 1:

@@ -40,13 +40,14 @@ def strided_partition_rows(tensor, world_size, rank, stride=1):
     chunks and rank ``r`` takes chunks ``r, r+world, r+2*world``
     (parallel/tensor_parallel.py:13-31).
     """
-    if tensor.dim() < 1:
-        raise ValueError("tensor must have a row dimension")
-    if world_size < 1 or not 0 <= rank < world_size:
-        raise ValueError("invalid TP rank/world size")
-    if stride < 1 or tensor.size(0) % (world_size * stride):
-        raise ValueError("rows must divide evenly by world_size * stride")
-    chunk = tensor.size(0) // (world_size * stride)
+    n_chunks = world_size * stride
+    ok = (tensor.dim() >= 1 and world_size >= 1 and 0 <= rank < world_size and stride >= 1
+          and tensor.size(0) % n_chunks == 0)
+    if not ok:
+        raise ValueError(f"cannot take TP shard {rank} of {world_size} (stride {stride}) from a tensor of shape "
+                         f"{tuple(tensor.shape)}: need a leading dimension that splits into world_size * stride "
+                         "equal chunks and 0 <= rank < world_size")
+    chunk = tensor.size(0) // n_chunks
     pieces = [tensor.narrow(0, (s * world_size + rank) * chunk, chunk) for s in range(stride)]
     return torch.cat(pieces, dim=0)
 

@@ -100,9 +100,11 @@ class TrainConfig:
     average_microbatches: bool = True   # False = reference PP semantics (sum of microbatch losses)
     seed: int = 42
     nvtx: bool = False                  # NVTX ranges per phase (also MMB_NVTX=1)
-    dp_early_buckets: bool = False      # launch DP buckets during backward (also MMB_DP_EARLY_BUCKETS=1)
+    dp_early_buckets: bool = True       # launch DP buckets during backward (MMB_DP_EARLY_BUCKETS=0 turns it off)
     cuda_graph: str = "auto"            # "on", "off", or "auto": replay each whole step as one CUDA graph
                                         # where supported (CUDA, tp = pp = dp = 1, flat fused AdamW)
+    error_check_interval: int = 20      # read the native kernels' device error word every N steps (0 = never;
+                                        # ``Trainer.check_device_errors`` checks on demand)
 
 
 class Trainer:
@@ -144,9 +146,10 @@ class Trainer:
         if impl == "auto":
             impl = "fused" if (self.device.type == "cuda" and dp > 1 and not sp) else "nccl"
         self.dp_impl = impl
+        self.dp_early = cfg.dp_early_buckets and os.environ.get("MMB_DP_EARLY_BUCKETS", "1") != "0"
         if impl == "fused":
             from .parallel.fused_dp import FusedDPOptimizer
-            early = cfg.dp_early_buckets or os.environ.get("MMB_DP_EARLY_BUCKETS") == "1"
+            early = self.dp_early
             self.optimizer = FusedDPOptimizer(self.model, mpu["dp_group"], lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                               weight_decay=cfg.weight_decay, bucket_elems=bucket_elems,
                                               overlap=cfg.dp_overlap, defer_done=early)
@@ -173,10 +176,10 @@ class Trainer:
                 layer._mmb_tp_ws = self.tp_ws
                 layer._mmb_tp_slot = i
         # Modules whose native backward announces "gradients final".  DP buckets launch strictly in
-        # order, head first, so the head and the embedding must be attached as well for any bucket to
-        # start during backward (MMB_DP_EARLY_BUCKETS=1; otherwise buckets start after backward).
+        # order, head first, so the head and the embedding are attached as well: buckets then start
+        # during backward (with MMB_DP_EARLY_BUCKETS=0 every bucket starts after backward).
         ready = list(layers)
-        if cfg.dp_early_buckets or os.environ.get("MMB_DP_EARLY_BUCKETS") == "1":
+        if self.dp_early:
             for name in ("embedding", "ln_f", "lm_head"):
                 mod = getattr(self.model, name, None)
                 if mod is not None:
@@ -211,8 +214,28 @@ class Trainer:
             self.tp_ws.poison()
         with _nvtx(self.nvtx, "train_step"):
             if self.graph_mode:
-                return self._graph_step(tokens, labels, loss_mask)
-            return self._train_step(tokens, labels, loss_mask)
+                out = self._graph_step(tokens, labels, loss_mask)
+            else:
+                out = self._train_step(tokens, labels, loss_mask)
+        n = self.cfg.error_check_interval
+        if n and self.step_count % n == 0:
+            self.check_device_errors()
+        return out
+
+    def check_device_errors(self):
+        """Raise if a native kernel recorded an error since the last check.
+
+        The fused TP/DP kernels bound every wait on a peer or an mbarrier; a
+        wait that runs out records an error code in a device word and the
+        kernel returns early, leaving that step's results incomplete (for the
+        fused DP kernel: parameters stale or partly updated on some ranks).
+        Reading the word synchronises the device, so it is read every
+        ``error_check_interval`` steps rather than after each one.
+        """
+        if self.device.type != "cuda":
+            return
+        from .ops import check_errors
+        check_errors()
 
     # ------------------------------------------------------------------ CUDA graphs
     GRAPH_WARMUP = 1
@@ -232,7 +255,7 @@ class Trainer:
         single = (self.mpu["dp_size"] == 1 and isinstance(self.optimizer, FusedAdamW) and not self.optimizer._loose)
         # the fused-DP step (no NCCL inside) with device-side epochs; gated with the early-bucket mode
         fused_dp = (self.dp_impl == "fused" and self.mpu["dp_size"] > 1 and not self.mpu["sequence_parallel"]
-                    and (cfg.dp_early_buckets or os.environ.get("MMB_DP_EARLY_BUCKETS") == "1"))
+                    and self.dp_early)
         supported = self.device.type == "cuda" and cfg.tp == 1 and cfg.pp == 1 and (single or fused_dp)
         if cfg.cuda_graph == "on" and not supported:
             raise ValueError("cuda_graph='on' needs CUDA, tp = pp = 1 and either dp = 1 with the flat fused AdamW "
@@ -350,6 +373,9 @@ class Trainer:
         return self.model, self.optimizer, self.scheduler
 
     def destroy(self):
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+            self.check_device_errors()
         self._graph = None
         if self.tp_ws is not None:
             self.tp_ws.close()

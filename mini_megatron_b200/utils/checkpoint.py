@@ -86,7 +86,15 @@ def _topology(mpu):
 
 
 def save_distributed_checkpoint(directory, model, optimizer, scheduler, step, mpu=None, sharded_optimizer=False):
+    """Write this rank's part of a distributed checkpoint.
+
+    The optimizer file is written per DP rank when ``sharded_optimizer`` is set
+    or when the optimizer itself reports that each DP rank holds only its own
+    slice of the state (``optimizer.state_is_sharded``: ZeRO-1 and the fused-DP
+    optimizer with dp > 1); otherwise DP rank 0 writes the one shared copy.
+    """
     os.makedirs(directory, exist_ok=True)
+    sharded_optimizer = bool(sharded_optimizer or getattr(optimizer, "state_is_sharded", False))
     model_name, optim_name = _names(mpu)
     dp_rank = mpu["dp_rank"] if mpu else 0
     written = {}

@@ -135,7 +135,7 @@ def bench_dp(args):
     model.weight = torch.nn.Parameter(torch.zeros(n, 1))
     model.cuda()
     opt = FusedDPOptimizer(model, None if world == 1 else dist.group.WORLD, lr=1e-4,
-                           bucket_elems=args.bucket_mb * (1 << 20) // 4, overlap=False)
+                           bucket_elems=args.bucket_mb * (1 << 20) // 4, overlap=False, defer_done=True)
     opt.buf.grad.normal_()
 
     def step():
@@ -143,8 +143,12 @@ def bench_dp(args):
         opt.step()
     ms = _time(step, args.iters)
     own = n / world
+    # A 2-D weight is a GEMM weight (kind 0): per element, the owner reads 4 B of gradient from each
+    # peer and writes 2 B of bf16 shadow into each peer, so every GPU sends (and receives)
+    # (world - 1) * own * 6 bytes.  HBM per GPU: its gradients read once (4n), the bf16 shadows
+    # written into it (2n), and the owned master and moments read and written (24 B per element).
     _report(rank, "dp_rs_adamw_ag", ms, nvlink_bytes=(world - 1) * own * 6.0,
-            hbm_bytes=own * (world * 4 + 4 * 3 + 4 * 3 + 2) + n * 6 / world * (world - 1),
+            hbm_bytes=6.0 * n + 24.0 * own,
             extra={"world": world, "params": n, "buckets": len(opt.buf.buckets)})
     torch.cuda.synchronize()
     check_errors()

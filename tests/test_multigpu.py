@@ -51,12 +51,12 @@ def _run(fn, world, *args, port=29711, env=None):
         return [torch.load(os.path.join(d, f"r{r}.pt"), weights_only=False) for r in range(world)]
 
 
-def _train(rank, world, tp, pp, sp, dp_impl, steps, micro, tp_impl="auto"):
+def _train(rank, world, tp, pp, sp, dp_impl, steps, micro, tp_impl="auto", recompute=False):
     from mini_megatron_b200.config import GPTConfig
     from mini_megatron_b200.training import TrainConfig, Trainer, synthetic_batch
     cfg = TrainConfig(model=GPTConfig(**CFG), micro_batch_size=2, seq_len=256, num_microbatches=micro, tp=tp, pp=pp,
                       sequence_parallel=sp, dp_impl=dp_impl, tp_impl=tp_impl, lr=1e-3, warmup_steps=0,
-                      num_steps=100, bucket_mb=1.0)
+                      num_steps=100, bucket_mb=1.0, recompute=recompute)
     t = Trainer(cfg)
     dp_rank = t.mpu["dp_rank"]
     losses = []
@@ -77,14 +77,17 @@ def _train(rank, world, tp, pp, sp, dp_impl, steps, micro, tp_impl="auto"):
 def test_fused_dp_matches_nccl_dp(early):
     """early: buckets start during backward (head and embedding hooks) and the bucket kernels defer
     their cross-rank completion wait to one wait at the end of the step."""
-    env = {"MMB_DP_EARLY_BUCKETS": "1"} if early else {}
+    env = {"MMB_DP_EARLY_BUCKETS": "1" if early else "0"}
     fused = _run(_train, 2, 1, 1, False, "fused", 3, 1, port=29711 + 10 * int(early), env=env)
     nccl = _run(_train, 2, 1, 1, False, "nccl", 3, 1, port=29712 + 10 * int(early), env=env)
     for r in range(2):
         for k, v in fused[r]["state"].items():
             ref = nccl[r]["state"][k]
             rel = ((v - ref).norm() / (ref.norm() + 1e-12)).item()
-            assert rel < 1e-4, (k, rel)
+            # the two paths sum the replicas' gradients in different orders; Adam's normalisation
+            # magnifies that rounding on tensors that are still near zero (LayerNorm biases start at 0
+            # and are ~1e-3 after three steps), so those are held to an absolute bound instead
+            assert rel < 1e-4 or (v - ref).abs().max().item() < 1e-6, (k, rel)
     # replicas agree with each other exactly (both received the same all-gathered parameters)
     for k in fused[0]["state"]:
         assert torch.equal(fused[0]["state"][k], fused[1]["state"][k]), k
@@ -139,3 +142,67 @@ def test_fused_tp_poisoned_workspace_gives_identical_results():
             ref = clean[r]["state"][k]
             assert torch.isfinite(v).all(), k
             assert ((v - ref).norm() / (ref.norm() + 1e-12)).item() < 1e-4, k
+
+
+@NEED2
+def test_fused_tp_recompute_matches():
+    """--recompute with the fused TP kernels: backward re-runs each layer's forward, including its
+    all-gather pushes and reduce-scatter, so the workspace epochs and slots must still line up."""
+    rc = _run(_train, 2, 2, 1, True, "nccl", 2, 2, "fused", True, port=29721)
+    ref = _run(_train, 2, 2, 1, True, "nccl", 2, 2, "fused", False, port=29722)
+    for r in range(2):
+        assert rc[r]["losses"][0] == ref[r]["losses"][0]
+        for a, b in zip(rc[r]["losses"], ref[r]["losses"]):
+            assert abs(a - b) <= 1e-3 * abs(b), (rc[r]["losses"], ref[r]["losses"])
+        for k, v in rc[r]["state"].items():
+            want = ref[r]["state"][k]
+            assert ((v - want).norm() / (want.norm() + 1e-12)).item() < 2e-3, k
+
+
+def _resume(rank, world, ckpt, phase):
+    """Fused DP (dp=2): phase 0 trains 2 steps, saves, trains 2 more; phase 1 loads and trains 2."""
+    from mini_megatron_b200.config import GPTConfig
+    from mini_megatron_b200.training import TrainConfig, Trainer, synthetic_batch
+    from mini_megatron_b200.utils.checkpoint import load_distributed_checkpoint, save_distributed_checkpoint
+    cfg = TrainConfig(model=GPTConfig(**CFG), micro_batch_size=2, seq_len=256, dp_impl="fused", lr=1e-3,
+                      warmup_steps=2, num_steps=20, bucket_mb=1.0)
+    t = Trainer(cfg)
+    dp_rank = t.mpu["dp_rank"]
+    losses = []
+
+    def run(steps):
+        for s in steps:
+            tok, lab = synthetic_batch(1, 2, 256, CFG["vocab_size"], seed=1000 * s + dp_rank)
+            losses.append(t.train_step(tok, lab).item())
+    if phase == 0:
+        run(range(2))
+        save_distributed_checkpoint(ckpt, *t.state_for_checkpoint(), 2, mpu=t.mpu)
+        run(range(2, 4))
+    else:
+        step = load_distributed_checkpoint(ckpt, *t.state_for_checkpoint(), mpu=t.mpu, device="cuda")
+        assert step == 2
+        run(range(2, 4))
+    state = {k: v.detach().float().cpu() for k, v in t.model.state_dict().items()}
+    t.destroy()
+    return {"losses": losses, "state": state}
+
+
+@NEED2
+def test_fused_dp_checkpoint_resume_continues_identically(tmp_path):
+    """Every DP rank writes its own optimizer shard (the fused-DP moments are sharded), and a run
+    resumed from the checkpoint continues with the same losses and parameters."""
+    ckpt = str(tmp_path / "ckpt")
+    full = _run(_resume, 2, ckpt, 0, port=29723)
+    import json
+    manifest = json.load(open(os.path.join(ckpt, "manifest.json")))
+    assert manifest["sharded_optimizer"] and len([f for f in manifest["files"] if f.startswith("optim")]) == 2
+    resumed = _run(_resume, 2, ckpt, 1, port=29724)
+    # split-K weight gradients and the attention dQ are summed with reduce-adds in no fixed order, so
+    # two runs agree to rounding, not bit for bit
+    for r in range(2):
+        for a, b in zip(resumed[r]["losses"], full[r]["losses"][2:]):
+            assert abs(a - b) < 1e-4 * abs(b), (resumed[r]["losses"], full[r]["losses"])
+        for k, v in resumed[r]["state"].items():
+            ref = full[r]["state"][k]
+            rel = ((v - ref).norm() / (ref.norm() + 1e-12)).item()
+            assert rel < 1e-4 or (v - ref).abs().max().item() < 1e-6, (k, rel)

@@ -153,3 +153,53 @@ def test_fused_ce_statistics_match_the_two_pass_head(monkeypatch):
     assert abs(out[True][0] - out[False][0]) < 1e-4 * abs(out[False][0])
     for n, g in out[True][1].items():
         assert _rel(g, out[False][1][n]) < 1e-3, n
+
+
+def test_native_recompute_matches_stored_activations():
+    """--recompute on the native path: each layer keeps only its input and re-runs its fused forward
+    inside backward.  The forward kernels are deterministic, so losses match and the parameters
+    after three steps agree to the order of the split-K / atomic reductions."""
+    from mini_megatron_b200.config import GPTConfig
+    from mini_megatron_b200.training import TrainConfig, Trainer, synthetic_batch
+    from mini_megatron_b200.parallel import process_groups as pg
+    mc = GPTConfig(num_layers=2, hidden_size=256, num_attention_heads=4, ffn_hidden_size=1024, max_seq_len=128,
+                   vocab_size=512)
+    runs = {}
+    for rc in (False, True):
+        cfg = TrainConfig(model=mc, micro_batch_size=4, seq_len=128, num_microbatches=2, lr=3e-3, warmup_steps=0,
+                          num_steps=20, recompute=rc, cuda_graph="off")
+        t = Trainer(cfg)
+        losses = []
+        for s in range(3):
+            tok, lab = synthetic_batch(2, 4, 128, 512, seed=s)
+            losses.append(t.train_step(tok, lab).item())
+        runs[rc] = (losses, {k: v.detach().float().clone() for k, v in t.model.state_dict().items()})
+        t.destroy()
+    assert runs[True][0][0] == runs[False][0][0]
+    for a, b in zip(runs[True][0], runs[False][0]):
+        assert abs(a - b) < 1e-3 * abs(b), (runs[True][0], runs[False][0])
+    for k, v in runs[True][1].items():
+        ref = runs[False][1][k]
+        assert _rel(v, ref) < 2e-3 or (v - ref).abs().max().item() < 1e-4, (k, _rel(v, ref))
+
+
+def test_trainer_raises_on_recorded_kernel_error():
+    """A bounded wait that ran out leaves its code in the device error word; the trainer reads the
+    word every ``error_check_interval`` steps and raises.  The error is written from the host, so
+    no kernel has to time out."""
+    from mini_megatron_b200.config import GPTConfig
+    from mini_megatron_b200.ops import native
+    from mini_megatron_b200.parallel import process_groups as pg
+    from mini_megatron_b200.training import TrainConfig, Trainer, synthetic_batch
+    mc = GPTConfig(num_layers=1, hidden_size=256, num_attention_heads=4, ffn_hidden_size=1024, max_seq_len=128,
+                   vocab_size=512)
+    t = Trainer(TrainConfig(model=mc, micro_batch_size=2, seq_len=128, warmup_steps=0, error_check_interval=2))
+    tok, lab = synthetic_batch(1, 2, 128, 512, seed=0)
+    t.train_step(tok, lab)
+    t.train_step(tok, lab)        # step 2: checked, clean
+    native().set_error(301)       # as dp_rs_adamw_ag would after a peer wait ran out
+    t.train_step(tok, lab)        # step 3: not a check step
+    with pytest.raises(RuntimeError, match="301"):
+        t.train_step(tok, lab)    # step 4: checked
+    assert native().get_error() == 0  # the check clears the word
+    pg.set_model_parallel(None)

@@ -29,7 +29,10 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
 
 
-@pytest.mark.parametrize("rows,H,with_dres", [(1000, 768, True), (333, 2048, False), (64, 4096, True)])
+# (8192, 4096): the regular path would use 512 partial rows, more than the 256 that fit in the fixed
+# scratch at H = 4096, so this case runs with fewer, taller bands than the regular binding.
+@pytest.mark.parametrize("rows,H,with_dres", [(1000, 768, True), (333, 2048, False), (64, 4096, True),
+                                              (8192, 4096, True)])
 def test_noalloc_matches_regular_entry_point(rows, H, with_dres):
     C, fn = _lib()
     torch.manual_seed(rows + H)
