@@ -309,7 +309,7 @@ void cast_f32_bf16(const Tensor& x, Tensor& y) {
 
 // ----------------------------------------------------------------- attention
 // qkv [B*S, 3*nh*d] bf16 (columns [Q heads | K heads | V heads]) -> (out [B*S, nh*d] bf16, lse [B, nh, S] fp32)
-std::vector<Tensor> flash_attn_fwd(const Tensor& qkv, int64_t B, int64_t S, int64_t nh, int64_t d) {
+std::vector<Tensor> flash_attn_fwd_impl(const Tensor& qkv, int64_t B, int64_t S, int64_t nh, int64_t d, bool v1) {
   check_cuda(qkv, "qkv");
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D bf16");
   TORCH_CHECK(qkv.size(0) == B * S && qkv.size(1) == 3 * nh * d, "qkv shape mismatch");
@@ -317,12 +317,22 @@ std::vector<Tensor> flash_attn_fwd(const Tensor& qkv, int64_t B, int64_t S, int6
   TORCH_CHECK(d == 64 || d == 128, "flash attention supports head_dim 64 and 128");
   Tensor out = at::empty({B * S, nh * d}, qkv.options());
   Tensor lse = at::empty({B, nh, S}, qkv.options().dtype(at::kFloat));
-  const int rc = mmb::flash_attn_fwd(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), (int)B,
-                                     (int)S, (int)nh, (int)d, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                     out.stride(0), lse.data_ptr<float>(), (float)(1.0 / std::sqrt((double)d)),
-                                     error_word(), cur_stream());
+  const auto* q = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  const float scale = (float)(1.0 / std::sqrt((double)d));
+  const int rc = v1 ? mmb::flash_attn_fwd(q, qkv.stride(0), (int)B, (int)S, (int)nh, (int)d, o, out.stride(0),
+                                          lse.data_ptr<float>(), scale, error_word(), cur_stream())
+                    : mmb::flash_attn_fwd_sm100(q, qkv.stride(0), (int)B, (int)S, (int)nh, (int)d, o, out.stride(0),
+                                                lse.data_ptr<float>(), scale, error_word(), num_sms(), cur_stream());
   MMB_CHECK_RC(rc, "flash_attn_fwd");
   return {out, lse};
+}
+
+std::vector<Tensor> flash_attn_fwd(const Tensor& qkv, int64_t B, int64_t S, int64_t nh, int64_t d) {
+  return flash_attn_fwd_impl(qkv, B, S, nh, d, false);
+}
+std::vector<Tensor> flash_attn_fwd_v1(const Tensor& qkv, int64_t B, int64_t S, int64_t nh, int64_t d) {
+  return flash_attn_fwd_impl(qkv, B, S, nh, d, true);
 }
 
 Tensor flash_attn_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse, int64_t B,
@@ -725,6 +735,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("EPI_PUSH_BF16") = (int)mmb::EPI_PUSH_BF16;
   m.def("num_sms", &num_sms);
   m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_fwd_v1", &flash_attn_fwd_v1, "previous one-tile-per-CTA forward (comparison only)");
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.attr("EPI_F32_ATOMIC") = (int)mmb::EPI_F32_ATOMIC;
   m.attr("EPI_BF16") = (int)mmb::EPI_BF16;

@@ -70,6 +70,8 @@ int cast_f32_bf16(const float* x, __nv_bfloat16* y, long n, int num_sms, cudaStr
 
 int flash_attn_fwd(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, int nh, int d, __nv_bfloat16* out,
                    long ld_out, float* lse, float softmax_scale, int* err, cudaStream_t stream);
+int flash_attn_fwd_sm100(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, int nh, int d, __nv_bfloat16* out,
+                         long ld_out, float* lse, float softmax_scale, int* err, int num_sms, cudaStream_t stream);
 int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* qkv, long ld_qkv,
                    const __nv_bfloat16* out, const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv,
                    long ld_dqkv, int B, int S, int nh, int d, float softmax_scale, int* err, int num_sms,

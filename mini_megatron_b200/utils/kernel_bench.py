@@ -3,6 +3,8 @@
 Usage::
 
     python -m mini_megatron_b200.utils.kernel_bench gemm [--model gpt-125m] [--tokens 16384]
+    python -m mini_megatron_b200.utils.kernel_bench attn      # causal attention vs torch SDPA
+    python -m mini_megatron_b200.utils.kernel_bench attn_case --d 64   # one fwd + bwd launch (ncu target)
 
 Each kernel is timed with CUDA events on the launching stream after warm-up,
 with a device synchronise on both sides; an L2-sized buffer is rewritten
@@ -66,6 +68,71 @@ def bench_gemm(args):
     assert _C.get_error() == 0
 
 
+def _attn_views(qkv, B, S, nh, d):
+    t = qkv.view(B, S, 3, nh, d)
+    return (t[:, :, 0].transpose(1, 2), t[:, :, 1].transpose(1, 2), t[:, :, 2].transpose(1, 2))
+
+
+def bench_attn(args):
+    """Causal attention forward and backward against torch SDPA (the reference's op) on the same GPU.
+
+    Shapes: GPT-125M (B=16, S=1024, 12 heads, d=64) and the d=128 long-sequence case
+    (B=4, S=2048, 16 heads, d=128).  Causal FLOPs: forward 2 * B * h * S^2 * d,
+    backward 2.5x that.
+    """
+    from mini_megatron_b200 import _C
+    import torch.nn.functional as F
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+    shapes = [(16, 1024, 12, 64), (4, 2048, 16, 128)]
+    for B, S, nh, d in shapes:
+        torch.manual_seed(0)
+        qkv = (torch.randn(B * S, 3 * nh * d, device="cuda") * 0.5).bfloat16()
+        dout = torch.randn(B * S, nh * d, device="cuda").bfloat16()
+        fl = 2.0 * B * nh * S * S * d
+        rec = {"kernel": "flash_attn", "B": B, "S": S, "heads": nh, "d": d, "fwd_gflop": round(fl / 1e9, 2)}
+        rec["fwd_ms"] = _timeit(lambda: _C.flash_attn_fwd(qkv, B, S, nh, d), flush=flush)
+        if hasattr(_C, "flash_attn_fwd_v1"):
+            rec["fwd_v1_ms"] = _timeit(lambda: _C.flash_attn_fwd_v1(qkv, B, S, nh, d), flush=flush)
+        o, lse = _C.flash_attn_fwd(qkv, B, S, nh, d)
+        rec["bwd_ms"] = _timeit(lambda: _C.flash_attn_bwd(dout, qkv, o, lse, B, S, nh, d), flush=flush)
+        q, k, v = _attn_views(qkv, B, S, nh, d)
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        rec["sdpa_fwd_ms"] = _timeit(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), flush=flush)
+        qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
+        out = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
+        go = dout.view(B, S, nh, d).transpose(1, 2).contiguous()
+        rec["sdpa_bwd_ms"] = _timeit(lambda: torch.autograd.grad(out, (qg, kg, vg), go, retain_graph=True),
+                                     flush=flush)
+        # numerics of this forward against SDPA's on the same inputs
+        ref = out.detach().transpose(1, 2).reshape(B * S, nh * d).float()
+        rec["fwd_max_abs_err_vs_sdpa"] = float((o.float() - ref).abs().max())
+        for key in ("fwd", "fwd_v1", "sdpa_fwd"):
+            if key + "_ms" in rec:
+                rec[key + "_tflops"] = round(fl / rec[key + "_ms"] / 1e9, 1)
+        for key in ("bwd", "sdpa_bwd"):
+            rec[key + "_tflops"] = round(2.5 * fl / rec[key + "_ms"] / 1e9, 1)
+        for k_ in list(rec):
+            if k_.endswith("_ms"):
+                rec[k_] = round(rec[k_], 4)
+        print(json.dumps(rec), flush=True)
+    assert _C.get_error() == 0
+
+
+def attn_case(args):
+    """One forward and one backward launch of the attention kernels (a small ncu target)."""
+    from mini_megatron_b200 import _C
+    B, S, nh, d = (16, 1024, 12, 64) if args.d == 64 else (4, 2048, 16, 128)
+    torch.manual_seed(0)
+    qkv = (torch.randn(B * S, 3 * nh * d, device="cuda") * 0.5).bfloat16()
+    dout = torch.randn(B * S, nh * d, device="cuda").bfloat16()
+    for _ in range(2):
+        o, lse = _C.flash_attn_fwd(qkv, B, S, nh, d)
+        _C.flash_attn_bwd(dout, qkv, o, lse, B, S, nh, d)
+        torch.cuda.synchronize()
+    assert _C.get_error() == 0
+    print("attention case done")
+
+
 def profile_case(args):
     """One launch of each hot kernel on GPT-125M training shapes (B=16, S=1024): the ncu target.
 
@@ -126,11 +193,12 @@ def profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "profile"])
+    ap.add_argument("kernel", choices=["gemm", "profile", "attn", "attn_case"])
     ap.add_argument("--model", default="gpt-125m")
     ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--d", type=int, default=64)
     args = ap.parse_args()
-    {"gemm": bench_gemm, "profile": profile_case}[args.kernel](args)
+    {"gemm": bench_gemm, "profile": profile_case, "attn": bench_attn, "attn_case": attn_case}[args.kernel](args)
 
 
 if __name__ == "__main__":
