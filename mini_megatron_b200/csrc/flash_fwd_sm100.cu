@@ -57,12 +57,18 @@ struct Cfg {
   static constexpr int CHUNKS = D / 64;           // 64-column (128 B) chunks per row
   static constexpr int TILE = BM * D * 2;         // bytes of one 128-row Q / K / V tile
   static constexpr int NS = (D == 64) ? 4 : 2;    // K/V ring stages
-  static constexpr int Q_OFF = 0;                 // Q0, Q1
-  static constexpr int K_OFF = 2 * TILE;
+  // d = 64: P has its own TMEM columns, so S_i(j+1) can be computed while the softmax of S_i(j)
+  // runs, and Q is double-buffered so the next item's tiles load during this one.  d = 128 has
+  // no TMEM left for that (S 2x128 + O 2x128 = 512 columns): P overwrites S and Q is single.
+  static constexpr bool SEP = (D == 64);
+  static constexpr int Q_BUFS = SEP ? 2 : 1;
+  static constexpr int Q_OFF = 0;                 // [Q_BUFS][Q0, Q1]
+  static constexpr int K_OFF = Q_BUFS * 2 * TILE;
   static constexpr int V_OFF = K_OFF + NS * TILE;
   static constexpr int BAR_OFF = V_OFF + NS * TILE;
   static constexpr int SMEM = 1024 + BAR_OFF + 512;
   static constexpr uint32_t T_S0 = 0, T_S1 = 128, T_O0 = 256, T_O1 = 256 + D;
+  static constexpr uint32_t T_P0 = SEP ? 384 : T_S0, T_P1 = SEP ? 448 : T_S1;
 };
 
 struct Args {
@@ -107,6 +113,13 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// One arrival per warp on `bar`, after every lane's tcgen05 loads / stores are ordered before it.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar) {
+  tc_fence_before();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 struct Item {
   int b, h, t0, t1;  // t0 < 0: the item has only tile t1 (odd number of query tiles)
 };
@@ -124,11 +137,13 @@ __device__ __forceinline__ Item decode(int item, int BH, int nh, int n_qt) {
 }
 
 template <int D>
-__global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers each
+__global__ void __launch_bounds__(kThreads, 1)  // 10 warps: 3 on some SM sub-partitions -> <= 168 registers
     flash_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_qkv, const Args a) {
   pdl_trigger();
   using C = Cfg<D>;
   constexpr int NS = C::NS;
+  constexpr int QB = C::Q_BUFS;
+  constexpr bool SEP = C::SEP;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -136,16 +151,18 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
   uint8_t* sK = smem + C::K_OFF;
   uint8_t* sV = smem + C::V_OFF;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;            // [NS]
+  uint64_t* q_full = bars + 0;            // [2]
+  uint64_t* q_empty = bars + 2;           // [2]
+  uint64_t* k_full = bars + 4;            // [NS]
   uint64_t* k_empty = k_full + NS;        // [NS]
   uint64_t* v_full = k_empty + NS;        // [NS]
   uint64_t* v_empty = v_full + NS;        // [NS]
   uint64_t* s_full = v_empty + NS;        // [2]  S_i computed
-  uint64_t* p_full = s_full + 2;          // [2]  P_i written (128 arrivals)
-  uint64_t* o_full = p_full + 2;          // [2]  last PV_i of the item complete
-  uint64_t* o_free = o_full + 2;          // [2]  O_i read by the epilogue (128 arrivals)
+  uint64_t* s_free = s_full + 2;          // [2]  S_i read into registers (SEP only; one arrival per warp)
+  uint64_t* p_full = s_free + 2;          // [2]  P_i written (one arrival per softmax warp)
+  uint64_t* p_free = p_full + 2;          // [2]  PV_i that read P_i complete (SEP only)
+  uint64_t* o_full = p_free + 2;          // [2]  last PV_i of the item complete
+  uint64_t* o_free = o_full + 2;          // [2]  O_i read by the epilogue (one arrival per softmax warp)
   uint64_t* drain = o_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -156,19 +173,21 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
   const int n_items = BH * ((n_qt + 1) / 2);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
     for (int s = 0; s < NS; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -195,12 +214,17 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
         const Item w = decode(item, BH, a.nh, n_qt);
         const int row0 = w.b * a.S;
         const int qx = a.q_col0 + w.h * D, kx = a.k_col0 + w.h * D, vx = a.v_col0 + w.h * D;
-        if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-        mbar_expect_tx(q_full, (w.t0 >= 0 ? 2 : 1) * C::TILE);
+        const int qb = it % QB;
+        if (it >= QB && !mbar_wait(&q_empty[qb], ((it / QB) - 1) & 1, a.err, kErrAttnWait, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint8_t* qd = sQ + qb * 2 * C::TILE;
+        mbar_expect_tx(&q_full[qb], (w.t0 >= 0 ? 2 : 1) * C::TILE);
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) {
-          if (w.t0 >= 0) tma_load_2d(sQ + c * 16384, &tm_qkv, q_full, qx + 64 * c, row0 + w.t0 * BM);
-          tma_load_2d(sQ + C::TILE + c * 16384, &tm_qkv, q_full, qx + 64 * c, row0 + w.t1 * BM);
+          if (w.t0 >= 0) tma_load_2d(qd + c * 16384, &tm_qkv, &q_full[qb], qx + 64 * c, row0 + w.t0 * BM);
+          tma_load_2d(qd + C::TILE + c * 16384, &tm_qkv, &q_full[qb], qx + 64 * c, row0 + w.t1 * BM);
         }
         q_issued = it;
         const int J = w.t1 + 1;
@@ -224,7 +248,7 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
       }
       if (!ok) {
         // let the loads this thread issued land before the CTA's shared memory goes away
-        if (q_issued >= 0) drain_wait(q_full, q_issued & 1);
+        for (int u = std::max(0, q_issued - QB + 1); u <= q_issued; ++u) drain_wait(&q_full[u % QB], (u / QB) & 1);
         for (int u = std::max(0, kv - NS); u < kv; ++u) {
           drain_wait(&k_full[u % NS], (u / NS) & 1);
           drain_wait(&v_full[u % NS], (u / NS) & 1);
@@ -236,80 +260,94 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BM, BN, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16(BM, D, false, true);
-      const uint32_t q0 = smem_u32(sQ), q1 = smem_u32(sQ + C::TILE);
       int kv = 0, it = 0;
-      int pc[2] = {0, 0};  // P tiles consumed per softmax group (p_full phases)
+      int sc[2] = {0, 0};  // S_i issued per group (s_free phases)
+      int pc[2] = {0, 0};  // P_i consumed per group (p_full phases)
       int ic[2] = {0, 0};  // items with an active tile per group (o_free phases)
       bool ok = true;
-      auto issue_s = [&](int i, int stage) {
-        const uint32_t qa = i == 0 ? q0 : q1;
-        const uint32_t ka = smem_u32(sK + stage * C::TILE);
+      // S_i = Q_i K^T into the S columns of group i (SEP: once the softmax has read the previous S_i)
+      auto issue_s = [&](int i, uint32_t qa, int stage) -> bool {
+        if (SEP && sc[i] > 0 && !mbar_wait(&s_free[i], (sc[i] - 1) & 1, a.err, kErrAttnWait, abort_flag))
+          return false;
+        ++sc[i];
+        tc_fence_after();
         const uint32_t dst = tmem + (i == 0 ? C::T_S0 : C::T_S1);
+        // the start-address field is (address >> 4) in the low 14 bits: per-step offsets are added to it
+        const uint64_t qd = make_sdesc_sw128(qa, 16, 1024);
+        const uint64_t kd = make_sdesc_sw128(smem_u32(sK + stage * C::TILE), 16, 1024);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_bf16_ss(dst, make_sdesc_sw128(qa + off, 16, 1024), make_sdesc_sw128(ka + off, 16, 1024), idesc_s,
-                       k != 0 ? 1u : 0u);
+          const uint32_t off16 = ((k >> 2) * 16384 + (k & 3) * 32) >> 4;
+          umma_bf16_ss(dst, qd + off16, kd + off16, idesc_s, k != 0 ? 1u : 0u);
         }
         umma_commit(&s_full[i]);
+        return true;
       };
-      auto issue_pv = [&](int i, int stage, bool acc) {
-        const uint32_t va = smem_u32(sV + stage * C::TILE);
-        const uint32_t p_t = tmem + (i == 0 ? C::T_S0 : C::T_S1);
+      // O_i (+)= P_i V once the softmax has written P_i (and, for the first tile of an item, once the
+      // previous item's epilogue has read O_i)
+      auto issue_pv = [&](int i, int stage, bool first, bool last) -> bool {
+        if (!mbar_wait(&p_full[i], pc[i] & 1, a.err, kErrAttnWait, abort_flag)) return false;
+        ++pc[i];
+        if (first && ic[i] > 0 && !mbar_wait(&o_free[i], (ic[i] - 1) & 1, a.err, kErrAttnWait, abort_flag))
+          return false;
+        tc_fence_after();
+        const uint64_t vd = make_sdesc_sw128(smem_u32(sV + stage * C::TILE), 16384, 1024);
+        const uint32_t p_t = tmem + (i == 0 ? C::T_P0 : C::T_P1);
         const uint32_t o_t = tmem + (i == 0 ? C::T_O0 : C::T_O1);
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k)
-          umma_bf16_ts(o_t, p_t + k * 8, make_sdesc_sw128(va + k * 2048, 16384, 1024), idesc_o,
-                       (acc || k != 0) ? 1u : 0u);
+          umma_bf16_ts(o_t, p_t + k * 8, vd + (uint64_t)(k * (2048 >> 4)), idesc_o, (!first || k != 0) ? 1u : 0u);
+        if (SEP) umma_commit(&p_free[i]);
+        if (last) umma_commit(&o_full[i]);
+        return true;
       };
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
         const Item w = decode(item, BH, a.nh, n_qt);
         const bool act0 = w.t0 >= 0;
         const int J = w.t1 + 1;
-        if (!mbar_wait(q_full, it & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+        const int qb = it % QB;
+        const uint32_t q0 = smem_u32(sQ + qb * 2 * C::TILE), q1 = q0 + C::TILE;
+        if (!mbar_wait(&q_full[qb], (it / QB) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
         if (!mbar_wait(&k_full[kv % NS], (kv / NS) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        if (act0) issue_s(0, kv % NS);
-        issue_s(1, kv % NS);
+        if (act0 && !issue_s(0, q0, kv % NS)) { ok = false; break; }
+        if (!issue_s(1, q1, kv % NS)) { ok = false; break; }
         umma_commit(&k_empty[kv % NS]);
         for (int j = 0; j < J && ok; ++j) {
           const int st = (kv + j) % NS, ph = ((kv + j) / NS) & 1;
           const int st1 = (kv + j + 1) % NS, ph1 = ((kv + j + 1) / NS) & 1;
-          if (!mbar_wait(&v_full[st], ph, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-          if (act0 && j <= w.t0) {
-            if (!mbar_wait(&p_full[0], pc[0] & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-            ++pc[0];
-            if (j == 0 && ic[0] > 0 && !mbar_wait(&o_free[0], (ic[0] - 1) & 1, a.err, kErrAttnWait, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_pv(0, st, j > 0);
-            if (j == w.t0) umma_commit(&o_full[0]);
-            if (j + 1 <= w.t0) {
+          const bool t0_now = act0 && j <= w.t0, t0_next = act0 && j + 1 <= w.t0;
+          if (SEP) {
+            // next scores first: they only need the softmax to have read the current ones
+            if (j + 1 < J) {
               if (!mbar_wait(&k_full[st1], ph1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-              tc_fence_after();
-              issue_s(0, st1);
+              if (t0_next && !issue_s(0, q0, st1)) { ok = false; break; }
+              if (!issue_s(1, q1, st1)) { ok = false; break; }
+              umma_commit(&k_empty[st1]);
             }
-          }
-          if (!mbar_wait(&p_full[1], pc[1] & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-          ++pc[1];
-          if (j == 0 && ic[1] > 0 && !mbar_wait(&o_free[1], (ic[1] - 1) & 1, a.err, kErrAttnWait, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(1, st, j > 0);
-          umma_commit(&v_empty[st]);
-          if (j == J - 1) umma_commit(&o_full[1]);
-          if (j + 1 < J) {
-            if (!mbar_wait(&k_full[st1], ph1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(1, st1);
-            umma_commit(&k_empty[st1]);
+            if (!mbar_wait(&v_full[st], ph, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+            if (t0_now && !issue_pv(0, st, j == 0, j == w.t0)) { ok = false; break; }
+            if (!issue_pv(1, st, j == 0, j == J - 1)) { ok = false; break; }
+            umma_commit(&v_empty[st]);
+          } else {
+            // P_i overwrites S_i: order PV0_j, S0_{j+1}, PV1_j, S1_{j+1} (tile 0's softmax overlaps tile 1's MMAs)
+            if (!mbar_wait(&v_full[st], ph, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+            if (t0_now) {
+              if (!issue_pv(0, st, j == 0, j == w.t0)) { ok = false; break; }
+              if (t0_next) {
+                if (!mbar_wait(&k_full[st1], ph1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+                if (!issue_s(0, q0, st1)) { ok = false; break; }
+              }
+            }
+            if (!issue_pv(1, st, j == 0, j == J - 1)) { ok = false; break; }
+            umma_commit(&v_empty[st]);
+            if (j + 1 < J) {
+              if (!mbar_wait(&k_full[st1], ph1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+              if (!issue_s(1, q1, st1)) { ok = false; break; }
+              umma_commit(&k_empty[st1]);
+            }
           }
         }
-        umma_commit(q_empty);  // every S MMA of this item has been issued
+        umma_commit(&q_empty[qb]);  // every S MMA of this item has been issued
         kv += J;
         if (act0) ++ic[0];
         ++ic[1];
@@ -326,9 +364,10 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
     const int r = q * 32 + lane;              // query row within the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t t_s = tmem + (grp == 0 ? C::T_S0 : C::T_S1) + lane_off;
+    const uint32_t t_p = tmem + (grp == 0 ? C::T_P0 : C::T_P1) + lane_off;
     const uint32_t t_o = tmem + (grp == 0 ? C::T_O0 : C::T_O1) + lane_off;
     const float sl2 = a.scale_log2;
-    int sc = 0, ic = 0;
+    int sc = 0, pc = 0, ic = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item w = decode(item, BH, a.nh, n_qt);
@@ -345,6 +384,7 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
         tmem_ld_32x32b_x32(t_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
         tmem_ld_32x32b_x32(t_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
         tmem_wait_ld();
+        if (SEP) warp_arrive(&s_free[grp]);  // the next S_i may now be computed into these columns
         if (j == t) {  // diagonal tile: key column c is visible to query row r iff c <= r
 #pragma unroll
           for (int c = 0; c < 128; ++c)
@@ -358,25 +398,19 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
         const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
         const bool need = mt > m + kRescaleLog2;
-        if (__any_sync(0xffffffffu, need)) {
-          const float m_new = need ? mt : m;
-          const float alpha = need ? ex2(m - m_new) : 1.f;
-          if (j > 0) {
-            // PV_i(j-1) is complete (it was issued before S_i(j)): rescale this row of O in place
-#pragma unroll 1
-            for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the 128 scores stay in registers
-              uint32_t o[16];
-              tmem_ld_32x32b_x16(t_o + c * 16, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-              tmem_st_32x32b_x16(t_o + c * 16, o);
-            }
-          }
-          l *= alpha;
-          m = m_new;
+        const bool any_need = __any_sync(0xffffffffu, need) != 0;
+        float alpha = 1.f;
+        if (need) {
+          alpha = ex2(m - mt);  // m = -inf on the first tile: alpha = 0
+          m = mt;
         }
-        // P = exp2(S * sl2 - m) as bf16 pairs over the first 64 columns of this row of S
+        if (SEP) {
+          // the PV that read the previous P_i (and last wrote O_i) must be complete
+          if (pc > 0 && !wwait(&p_free[grp], (pc - 1) & 1, a.err, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+        }
+        ++pc;
+        // P = exp2(S * sl2 - m) as bf16 pairs (64 TMEM columns: SEP its own, else over the first half of S)
         float rs[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) rs[k] = 0.f;
@@ -391,12 +425,24 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
             rs[e & 7] += p0 + p1;
             pk[e] = pack_bf16x2(p0, p1);
           }
-          tmem_st_x32(t_s + hcol * 32, pk);
+          tmem_st_x32(t_p + hcol * 32, pk);
+        }
+        l = l * alpha + (((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7])));
+        if (any_need && j > 0) {
+          // PV_i(j-1) is complete (SEP: waited above; otherwise it was issued before S_i(j)):
+          // rescale this row of O in place before PV_i(j) adds the new tile
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(t_o + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_x32(t_o + c * 32, o);
+          }
         }
         tmem_wait_st();
-        l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
-        tc_fence_before();
-        mbar_arrive(&p_full[grp]);
+        warp_arrive(&p_full[grp]);
       }
       if (!ok) break;
       // epilogue: O / l -> bf16 row, LSE
@@ -422,8 +468,7 @@ __global__ void __maxnreg__(200)  // 10 warps on one SM: up to 204 registers eac
         }
       }
       a.lse[((size_t)w.b * a.nh + w.h) * a.S + (size_t)t * BM + r] = m * 0.69314718055994531f + logf(l);
-      tc_fence_before();
-      mbar_arrive(&o_free[grp]);
+      warp_arrive(&o_free[grp]);
     }
   }
 

@@ -250,6 +250,9 @@ def main(argv=None):
     ap.add_argument("--impl-b", default="ours", choices=("reference", "ours"))
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     ap.add_argument("--amp", action="store_true", help="bf16 autocast for the reference implementation")
+    ap.add_argument("--amp-b", action="store_true",
+                    help="bf16 autocast for impl b only (e.g. the reference in fp32 against itself under autocast)")
+    ap.add_argument("--no-tf32", action="store_true", help="full fp32 matmuls for the fp32 reference (no TF32)")
     ap.add_argument("--preset", default="gpt-125m")
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--batch-size", type=int, default=2)
@@ -270,13 +273,17 @@ def main(argv=None):
         os.environ.setdefault("MASTER_PORT", str(29400 + os.getpid() % 500))
         dist.init_process_group("gloo", rank=0, world_size=1)
     torch.manual_seed(args.seed)
+    if args.no_tf32:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.backends.cudnn.allow_tf32 = False
     a = build_impl(args.impl_a, mc, device, args.amp)
-    b = build_impl(args.impl_b, mc, device, args.amp)
+    b = build_impl(args.impl_b, mc, device, args.amp or args.amp_b)
     tokens, labels, mask = fixed_batch(args.batch_size, mc["max_seq_len"], mc["vocab_size"], args.seed + 1)
     rep = run_parity(a, b, mc, tokens, labels, mask, device)
     native = any(k == "ours" for k in (args.impl_a, args.impl_b)) and device.type == "cuda"
-    gate_name = args.gate or ("bf16" if (native or args.amp) else "fp32")
+    gate_name = args.gate or ("bf16" if (native or args.amp or args.amp_b) else "fp32")
     rep.update({"impl_a": args.impl_a, "impl_b": args.impl_b, "device": str(device), "amp": args.amp,
+                "amp_b": args.amp_b, "tf32": not args.no_tf32,
                 "model": mc, "gate_name": gate_name, "gate": GATES[gate_name],
                 "checks": evaluate(rep, GATES[gate_name])})
     rep["passed"] = rep["checks"]["passed"]
