@@ -144,9 +144,14 @@ class Trainer:
         grad_scale = 1.0 / dp
         impl = cfg.dp_impl
         if impl == "auto":
-            impl = "fused" if (self.device.type == "cuda" and dp > 1 and not sp) else "nccl"
+            impl = "fused" if (self.device.type == "cuda" and dp > 1) else "nccl"
         self.dp_impl = impl
         self.dp_early = cfg.dp_early_buckets and os.environ.get("MMB_DP_EARLY_BUCKETS", "1") != "0"
+        if impl == "fused" and sp:
+            # The fused kernel applies AdamW as soon as a bucket's gradients are final across the DP
+            # group, but sequence-parallel LayerNorm gradients are only complete after their TP
+            # all-reduce at the end of backward: every bucket then starts after that reduction.
+            self.dp_early = False
         if impl == "fused":
             from .parallel.fused_dp import FusedDPOptimizer
             early = self.dp_early
@@ -178,7 +183,7 @@ class Trainer:
         # Modules whose native backward announces "gradients final".  DP buckets launch strictly in
         # order, head first, so the head and the embedding are attached as well: buckets then start
         # during backward (with MMB_DP_EARLY_BUCKETS=0 every bucket starts after backward).
-        ready = list(layers)
+        ready = [] if (self.dp_impl == "fused" and sp) else list(layers)
         if self.dp_early:
             for name in ("embedding", "ln_f", "lm_head"):
                 mod = getattr(self.model, name, None)
