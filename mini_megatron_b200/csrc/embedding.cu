@@ -41,57 +41,97 @@ __global__ void emb_fwd_kernel(const long* __restrict__ ids, const float* __rest
 
 // Token-table gradient with per-row ownership (deterministic, no atomics).
 //
-// Warp w of the grid owns the table rows [w * R, (w + 1) * R).  Each CTA streams
-// the token ids through shared memory in chunks of 256 positions (stored as
-// the row in this vocabulary shard, or -1); every warp scans the chunk 32
-// positions at a time and, for each distinct owned row among them, adds the
-// sum of those positions' gradient rows (in position order) to its row of the
-// main grad.  Every element is therefore summed in one fixed order, run after
-// run, unlike a scatter with atomics.
-constexpr int kEmbChunk = 256;
+// CTA c owns the table rows [c * R, (c + 1) * R) of this vocabulary shard.  It
+// reads every token id once (thread t takes a contiguous run of positions, so
+// a block-wide exclusive scan of the per-thread match counts lays the matching
+// positions out in shared memory in increasing position order), then warp w
+// walks that list and handles the rows with row % 8 == w: for each distinct row
+// among 32 consecutive entries it adds the sum of those positions' gradient
+// rows, in position order, to the row of the main grad.  Every element is thus
+// summed in one fixed order, run after run.  The list holds kEmbList entries;
+// a CTA with more matches (a very skewed batch) handles its positions in
+// several windows, still in order.
+constexpr int kEmbList = 4096;
+constexpr int kEmbThreads = 256;
 
-__global__ void __launch_bounds__(256) emb_bwd_tok_kernel(const long* __restrict__ ids,
-                                                          const float* __restrict__ dout, float* __restrict__ dwte,
-                                                          int rows, int H, long vstart, long vend, int rows_per_warp) {
+__global__ void __launch_bounds__(kEmbThreads) emb_bwd_tok_kernel(const long* __restrict__ ids,
+                                                                  const float* __restrict__ dout,
+                                                                  float* __restrict__ dwte, int rows, int H,
+                                                                  long vstart, long vend, int rows_per_cta) {
   pdl_trigger();
   pdl_wait();
-  __shared__ int rel[kEmbChunk];
-  const int lane = threadIdx.x & 31;
-  const long gw = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const long lo = gw * rows_per_warp;
-  const long hi = min(lo + rows_per_warp, vend - vstart);
+  __shared__ int list_pos[kEmbList];
+  __shared__ int list_row[kEmbList];
+  __shared__ int warp_tot[kEmbThreads / 32];
+  __shared__ int total_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long lo = (long)blockIdx.x * rows_per_cta;
+  const long hi = min(lo + rows_per_cta, vend - vstart);
+  if (lo >= hi) return;
   const int h4 = H / 4;
-  for (int base = 0; base < rows; base += kEmbChunk) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < kEmbChunk; i += blockDim.x) {
-      const int r = base + i;
-      const long id = r < rows ? ids[r] : -1;
-      rel[i] = (id >= vstart && id < vend) ? (int)(id - vstart) : -1;
+  // positions per window: each thread scans `per` consecutive positions of the window
+  const int per = (kEmbList + kEmbThreads - 1) / kEmbThreads;  // at most kEmbList matches per window
+  const int win = per * kEmbThreads;
+  for (int w0 = 0; w0 < rows; w0 += win) {
+    const int p0 = w0 + tid * per;
+    int cnt = 0;
+    for (int k = 0; k < per; ++k) {
+      const int p = p0 + k;
+      if (p < rows) {
+        const long v = ids[p] - vstart;
+        cnt += (v >= lo && v < hi) ? 1 : 0;
+      }
     }
+    // block-wide exclusive scan of the counts (warp shuffles, then the 8 warp totals)
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
     __syncthreads();
-    if (lo >= hi) continue;
-    for (int sub = 0; sub < kEmbChunk; sub += 32) {
-      const int v = rel[sub + lane];
-      unsigned mask = __ballot_sync(0xffffffffu, v >= lo && v < hi);
-      while (mask) {
-        const int src = __ffs(mask) - 1;
-        const int row = __shfl_sync(0xffffffffu, v, src);
-        const unsigned same = __ballot_sync(0xffffffffu, v == row) & mask;
-        mask &= ~same;
-        float4* w = reinterpret_cast<float4*>(dwte + (size_t)row * H);
-        for (int c = lane; c < h4; c += 32) {
-          float4 acc = w[c];
-          unsigned m2 = same;
-          while (m2) {  // positions in increasing order
-            const int k = __ffs(m2) - 1;
-            m2 &= m2 - 1;
-            const float4 d = reinterpret_cast<const float4*>(dout + (size_t)(base + sub + k) * H)[c];
-            acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
-          }
-          w[c] = acc;
+    int off = incl - cnt;
+    for (int w = 0; w < warp; ++w) off += warp_tot[w];
+    if (tid == kEmbThreads - 1) total_s = off + cnt;
+    for (int k = 0; k < per && cnt > 0; ++k) {
+      const int p = p0 + k;
+      if (p < rows) {
+        const long v = ids[p] - vstart;
+        if (v >= lo && v < hi) {
+          list_pos[off] = p;
+          list_row[off] = (int)v;
+          ++off;
         }
       }
     }
+    __syncthreads();
+    const int total = total_s;
+    // warp `warp` owns the rows with row % 8 == warp; entries are in increasing position order
+    for (int b = 0; b < total; b += 32) {
+      const int e = b + lane;
+      const int row = e < total ? list_row[e] : -1;
+      unsigned mask = __ballot_sync(0xffffffffu, row >= 0 && (row & 7) == warp);
+      while (mask) {
+        const int src = __ffs(mask) - 1;
+        const int r = __shfl_sync(0xffffffffu, row, src);
+        const unsigned same = __ballot_sync(0xffffffffu, row == r) & mask;
+        mask &= ~same;
+        float4* wrow = reinterpret_cast<float4*>(dwte + (size_t)r * H);
+        for (int c = lane; c < h4; c += 32) {
+          float4 acc = wrow[c];
+          unsigned m2 = same;
+          while (m2) {
+            const int k = __ffs(m2) - 1;
+            m2 &= m2 - 1;
+            const float4 d = reinterpret_cast<const float4*>(dout + (size_t)list_pos[b + k] * H)[c];
+            acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+          }
+          wrow[c] = acc;
+        }
+      }
+    }
+    __syncthreads();  // the list is rebuilt for the next window
   }
 }
 
@@ -121,9 +161,9 @@ int embedding_bwd(const long* ids, const float* dout, float* dwte, float* dwpe, 
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long vrows = vend - vstart;
-  const int grid = (int)std::max<long>(1, std::min<long>(4L * sms, (vrows + 7) / 8));
-  const int rows_per_warp = (int)((vrows + 8L * grid - 1) / (8L * grid));
-  launch_k(emb_bwd_tok_kernel, grid, 256, 0, s, ids, dout, dwte, rows, H, vstart, vend, rows_per_warp);
+  const int grid = (int)std::max<long>(1, std::min<long>(2L * sms, (vrows + 63) / 64));
+  const int rows_per_cta = (int)((vrows + grid - 1) / grid);
+  launch_k(emb_bwd_tok_kernel, grid, kEmbThreads, 0, s, ids, dout, dwte, rows, H, vstart, vend, rows_per_cta);
   if (dwpe) launch_k(emb_bwd_pos_kernel, S, 256, 0, s, dout, dwpe, B, S, H);
   return (int)cudaGetLastError();
 }
