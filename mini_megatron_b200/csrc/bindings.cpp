@@ -335,8 +335,8 @@ std::vector<Tensor> flash_attn_fwd_v1(const Tensor& qkv, int64_t B, int64_t S, i
   return flash_attn_fwd_impl(qkv, B, S, nh, d, true);
 }
 
-Tensor flash_attn_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse, int64_t B,
-                      int64_t S, int64_t nh, int64_t d) {
+Tensor flash_attn_bwd_impl(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse, int64_t B,
+                           int64_t S, int64_t nh, int64_t d, bool v1) {
   check_bf16(dout, "dout");
   check_bf16(out, "out");
   check_f32(lse, "lse");
@@ -351,9 +351,18 @@ Tensor flash_attn_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, 
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), delta.data_ptr<float>(),
       dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), dqkv.stride(0), (int)B, (int)S,
-      (int)nh, (int)d, (float)(1.0 / std::sqrt((double)d)), error_word(), num_sms(), cur_stream());
+      (int)nh, (int)d, (float)(1.0 / std::sqrt((double)d)), error_word(), num_sms(), cur_stream(), v1);
   MMB_CHECK_RC(rc, "flash_attn_bwd");
   return dqkv;
+}
+
+Tensor flash_attn_bwd(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse, int64_t B,
+                      int64_t S, int64_t nh, int64_t d) {
+  return flash_attn_bwd_impl(dout, qkv, out, lse, B, S, nh, d, false);
+}
+Tensor flash_attn_bwd_v1(const Tensor& dout, const Tensor& qkv, const Tensor& out, const Tensor& lse, int64_t B,
+                         int64_t S, int64_t nh, int64_t d) {
+  return flash_attn_bwd_impl(dout, qkv, out, lse, B, S, nh, d, true);
 }
 
 // ----------------------------------------------------------------- symmetric memory
@@ -737,6 +746,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_fwd_v1", &flash_attn_fwd_v1, "previous one-tile-per-CTA forward (comparison only)");
   m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("flash_attn_bwd_v1", &flash_attn_bwd_v1, "one-key-tile-per-CTA backward (comparison only)");
   m.attr("EPI_F32_ATOMIC") = (int)mmb::EPI_F32_ATOMIC;
   m.attr("EPI_BF16") = (int)mmb::EPI_BF16;
   m.attr("EPI_F32") = (int)mmb::EPI_F32;

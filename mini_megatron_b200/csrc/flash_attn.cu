@@ -792,7 +792,7 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ dq, long ld_dq,
 int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* qkv, long ld_qkv,
                    const __nv_bfloat16* out, const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv,
                    long ld_dqkv, int B, int S, int nh, int d, float softmax_scale, int* err, int num_sms,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, bool one_tile_per_cta) {
   using namespace attn;
   if (S % BM != 0 || (d != 64 && d != 128)) return -1;
   if (ld_do != (long)nh * d) return -2;
@@ -803,6 +803,16 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
     launch_k(attn_delta_kernel, (unsigned)((threads + 255) / 256), 256, 0, stream, dout, out, ld_do, B, S, nh, d, delta);
   }
   cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * nh * d, stream);
+  const long n4 = rows * nh * d / 4;
+  if (d == 64 && !one_tile_per_cta) {
+    // persistent key/value-stationary kernel (flash_bwd_sm100.cu)
+    const int rc = flash_attn_bwd_sm100_d64(dout, ld_do, qkv, ld_qkv, lse, delta, dq_acc, dqkv, ld_dqkv, B, S, nh,
+                                            softmax_scale, err, num_sms, stream);
+    if (rc) return rc;
+    launch_k(attn_dq_convert_kernel, (unsigned)std::min<long>((n4 + 255) / 256, (long)num_sms * 8), 256, 0, stream,
+             dq_acc, (long)nh * d, dqkv, ld_dqkv, rows, nh * d);
+    return (int)cudaGetLastError();
+  }
   CUtensorMap tm_qkv, tm_do;
   int rc = make_tmap_bf16_2d(&tm_qkv, qkv, rows, 3L * nh * d, ld_qkv, 64, BM);
   if (rc) return rc - 10;
@@ -845,7 +855,6 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
     }
     launch_k(k, grid, kBwdThreads, BwdCfg<128>::SMEM, stream, tm_qkv, tm_do, tm_dq, a);
   }
-  const long n4 = rows * nh * d / 4;
   launch_k(attn_dq_convert_kernel, (unsigned)std::min<long>((n4 + 255) / 256, (long)num_sms * 8), 256, 0, stream, 
       dq_acc, (long)nh * d, dqkv, ld_dqkv, rows, nh * d);
   return (int)cudaGetLastError();

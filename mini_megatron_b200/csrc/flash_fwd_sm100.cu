@@ -99,11 +99,11 @@ __device__ __forceinline__ void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[
       : "memory");
 }
 
-// Warp-uniform bounded wait: lane 0 polls, the result is broadcast.
+// Warp-wide bounded wait: every lane polls the barrier (cheaper than one lane polling while
+// the others wait on a shuffle); the warp proceeds only if every lane saw the phase complete.
 __device__ __forceinline__ bool wwait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, err, kErrAttnWait, abort_flag) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  const bool ok = mbar_wait(bar, parity, err, kErrAttnWait, abort_flag);
+  return __all_sync(0xffffffffu, ok) != 0;
 }
 
 // Bounded wait used while winding down after an abort (does not look at the abort flag).

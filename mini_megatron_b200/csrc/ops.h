@@ -75,7 +75,10 @@ int flash_attn_fwd_sm100(const __nv_bfloat16* qkv, long ld_qkv, int B, int S, in
 int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* qkv, long ld_qkv,
                    const __nv_bfloat16* out, const float* lse, float* delta, float* dq_acc, __nv_bfloat16* dqkv,
                    long ld_dqkv, int B, int S, int nh, int d, float softmax_scale, int* err, int num_sms,
-                   cudaStream_t stream);
+                   cudaStream_t stream, bool one_tile_per_cta = false);
+int flash_attn_bwd_sm100_d64(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* qkv, long ld_qkv,
+                             const float* lse, const float* delta, float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv,
+                             int B, int S, int nh, float softmax_scale, int* err, int num_sms, cudaStream_t stream);
 
 // Fused DP step (fused_dp.cu)
 struct DpPeersHost {

@@ -95,6 +95,8 @@ def bench_attn(args):
             rec["fwd_v1_ms"] = _timeit(lambda: _C.flash_attn_fwd_v1(qkv, B, S, nh, d), flush=flush)
         o, lse = _C.flash_attn_fwd(qkv, B, S, nh, d)
         rec["bwd_ms"] = _timeit(lambda: _C.flash_attn_bwd(dout, qkv, o, lse, B, S, nh, d), flush=flush)
+        if hasattr(_C, "flash_attn_bwd_v1"):
+            rec["bwd_v1_ms"] = _timeit(lambda: _C.flash_attn_bwd_v1(dout, qkv, o, lse, B, S, nh, d), flush=flush)
         q, k, v = _attn_views(qkv, B, S, nh, d)
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         rec["sdpa_fwd_ms"] = _timeit(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), flush=flush)
@@ -109,8 +111,9 @@ def bench_attn(args):
         for key in ("fwd", "fwd_v1", "sdpa_fwd"):
             if key + "_ms" in rec:
                 rec[key + "_tflops"] = round(fl / rec[key + "_ms"] / 1e9, 1)
-        for key in ("bwd", "sdpa_bwd"):
-            rec[key + "_tflops"] = round(2.5 * fl / rec[key + "_ms"] / 1e9, 1)
+        for key in ("bwd", "bwd_v1", "sdpa_bwd"):
+            if key + "_ms" in rec:
+                rec[key + "_tflops"] = round(2.5 * fl / rec[key + "_ms"] / 1e9, 1)
         for k_ in list(rec):
             if k_.endswith("_ms"):
                 rec[k_] = round(rec[k_], 4)
