@@ -333,28 +333,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wwait(st_full, qi & 1, a.err, abort_flag)) { ok = false; break; }
         if (!wwait(&q_full[st], (qi / QS) & 1, a.err, abort_flag)) { ok = false; break; }  // LSE / Delta rows
         tc_fence_after();
-        uint32_t sv[64], dv[64];
-        tmem_ld_32x32b_x32(tmem + T_ST + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld_32x32b_x32(tmem + T_ST + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld_32x32b_x32(tmem + T_DPT + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
-        tmem_ld_32x32b_x32(tmem + T_DPT + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
-        tmem_wait_ld();
-        warp_arrive(st_free);  // the next tile's S^T / dP^T may now be computed
         const float* lse = sLD + st * 256 + half * 64;
         const float* dlt = lse + 128;
         const bool diag = (i == 0);
         uint32_t pp[32], dd[32];
+        // two passes of 32 query columns keep the live registers near 128 (no spills at 168)
 #pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          const int qc = half * 64 + e;  // query column within the tile
-          float p0 = ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse[e] * 1.4426950408889634f));
-          float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), sl2, -lse[e + 1] * 1.4426950408889634f));
-          if (diag && qc < c) p0 = 0.f;
-          if (diag && qc + 1 < c) p1 = 0.f;
-          const float d0 = p0 * (__uint_as_float(dv[e]) - dlt[e]);
-          const float d1 = p1 * (__uint_as_float(dv[e + 1]) - dlt[e + 1]);
-          pp[e >> 1] = pack_bf16x2(p0, p1);
-          dd[e >> 1] = pack_bf16x2(d0, d1);
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t sv[32], dv[32];
+          tmem_ld_32x32b_x32(tmem + T_ST + lane_off + half * 64 + hh * 32, sv);
+          tmem_ld_32x32b_x32(tmem + T_DPT + lane_off + half * 64 + hh * 32, dv);
+          tmem_wait_ld();
+          if (hh == 1) warp_arrive(st_free);  // the next tile's S^T / dP^T may now be computed
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const int col = hh * 32 + e;       // column within this warp's 64
+            const int qc = half * 64 + col;    // query column within the tile
+            float p0 = ex2(fmaf(__uint_as_float(sv[e]), sl2, -lse[col] * 1.4426950408889634f));
+            float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), sl2, -lse[col + 1] * 1.4426950408889634f));
+            if (diag && qc < c) p0 = 0.f;
+            if (diag && qc + 1 < c) p1 = 0.f;
+            const float d0 = p0 * (__uint_as_float(dv[e]) - dlt[col]);
+            const float d1 = p1 * (__uint_as_float(dv[e + 1]) - dlt[col + 1]);
+            pp[col >> 1] = pack_bf16x2(p0, p1);
+            dd[col >> 1] = pack_bf16x2(d0, d1);
+          }
         }
         // the previous tile's dV/dK/dQ MMAs must be done reading P^T and dS^T; within an item, its dQ
         // is drained here (the last tile of an item was waited for and drained at the item's end)
