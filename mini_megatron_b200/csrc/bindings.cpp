@@ -541,10 +541,35 @@ void tp_rs_reduce(int64_t slots_ptr, int64_t slot_stride, int64_t world, int64_t
                "tp_rs_reduce");
 }
 
+// Cross-entropy statistics across the TP group over NVLink: push this rank's (max, sumexp,
+// target) triplets into every peer's slots, then reduce all sources into (lse, target logit).
+std::vector<Tensor> tp_ce_allreduce(const Tensor& mx, const Tensor& se, const Tensor& tg,
+                                    const std::vector<int64_t>& dst, const std::vector<int64_t>& flags, int64_t rank,
+                                    int64_t epoch, Tensor& counter, int64_t slots_local, int64_t flags_local,
+                                    int64_t timeout_ms) {
+  check_f32(mx, "mx");
+  check_f32(se, "se");
+  check_f32(tg, "tg");
+  const int rows = (int)mx.numel();
+  TORCH_CHECK(se.numel() == rows && tg.numel() == rows, "tp_ce_allreduce: shapes");
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, 1, 1, 4, counter);
+  Tensor lse = at::empty_like(mx), tgo = at::empty_like(mx);
+  MMB_CHECK_RC(mmb::tp_ce_allreduce(mx.data_ptr<float>(), se.data_ptr<float>(), tg.data_ptr<float>(), rows, P,
+                                    reinterpret_cast<const void*>(slots_local),
+                                    reinterpret_cast<const int*>(flags_local), lse.data_ptr<float>(),
+                                    tgo.data_ptr<float>(), error_word(), num_sms(), cur_stream(),
+                                    (unsigned long long)timeout_ms * 1000000ull),
+               "tp_ce_allreduce");
+  return {lse, tgo};
+}
+
 // lm_head GEMM whose epilogue also writes per-tile cross-entropy partials, then the
 // merge: returns (max, sumexp, target logit) per row like ce_fwd_stats.
+// With ag_flags != 0 the rows of A are a sequence-parallel all-gather in progress: the GEMM's
+// TMA producer waits per source rank (flags >= ag_epoch) before loading that rank's rows.
 std::vector<Tensor> gemm_ce_stats(const Tensor& A, const Tensor& B, Tensor& D, const Tensor& labels,
-                                  int64_t vocab_start, int64_t n_valid) {
+                                  int64_t vocab_start, int64_t n_valid, int64_t ag_flags, int64_t ag_epoch,
+                                  int64_t S, int64_t Sl, int64_t rank) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   check_bf16(D, "D");
@@ -572,6 +597,14 @@ std::vector<Tensor> gemm_ce_stats(const Tensor& A, const Tensor& B, Tensor& D, c
   p.args.ce_part = reinterpret_cast<float2*>(part.data_ptr<float>());
   p.args.ce_ld = nparts;
   p.args.ce_n_valid = (int)n_valid;
+  if (ag_flags != 0) {
+    TORCH_CHECK(Sl % 128 == 0 && S % Sl == 0 && M % S == 0, "gemm_ce_stats: all-gather shards must be 128-row tiles");
+    p.args.ag_flags = reinterpret_cast<const int*>(ag_flags);
+    p.args.ag_epoch = (int)ag_epoch;
+    p.args.ag_S = (int)S;
+    p.args.ag_Sl = (int)Sl;
+    p.args.ag_rank = (int)rank;
+  }
   MMB_CHECK_RC(mmb::gemm_bf16_launch(p, cur_stream()), "gemm_ce_stats");
   Tensor mx = at::empty({M}, A.options().dtype(at::kFloat));
   Tensor se = at::empty_like(mx), tg = at::empty_like(mx);
@@ -618,6 +651,7 @@ void gemm_tp(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, const c10::
     p.args.ag_epoch = (int)ag_epoch;
     p.args.ag_S = (int)S;
     p.args.ag_Sl = (int)Sl;
+    p.args.ag_rank = (int)rank;
   }
   if (epi == mmb::EPI_PUSH_BF16) {
     TORCH_CHECK(push_dst.size() == push_flags.size() && push_dst.size() >= 1 && push_dst.size() <= 8, "push ranks");
@@ -697,7 +731,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gamma"), py::arg("dres"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"),
         py::arg("dx_bf16") = c10::nullopt);
   m.def("ce_fwd_stats", &ce_fwd_stats);
-  m.def("gemm_ce_stats", &gemm_ce_stats, "lm_head GEMM with cross-entropy statistics fused into its epilogue");
+  m.def("gemm_ce_stats", &gemm_ce_stats, "lm_head GEMM with cross-entropy statistics fused into its epilogue",
+        py::arg("A"), py::arg("B"), py::arg("D"), py::arg("labels"), py::arg("vocab_start"), py::arg("n_valid"),
+        py::arg("ag_flags") = 0, py::arg("ag_epoch") = 0, py::arg("S") = 0, py::arg("Sl") = 0, py::arg("rank") = 0);
+  m.def("tp_ce_allreduce", &tp_ce_allreduce, py::arg("mx"), py::arg("se"), py::arg("tg"), py::arg("dst"),
+        py::arg("flags"), py::arg("rank"), py::arg("epoch"), py::arg("counter"), py::arg("slots_local"),
+        py::arg("flags_local"), py::arg("timeout_ms") = 10000);
   m.def("ce_bwd", &ce_bwd);
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);

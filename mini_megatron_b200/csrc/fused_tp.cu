@@ -88,6 +88,57 @@ __global__ void __launch_bounds__(256) tp_ag_push_kernel(const __nv_bfloat16* __
   grid_done_signal(P.flags, P.world, P.rank, P.epoch, P.counter);
 }
 
+// Vocabulary-parallel cross-entropy statistics across the TP group: every rank
+// holds (row max, sum of exp(logit - max), target logit or 0) of its vocabulary
+// shard for every token row.  Push: each rank writes its triplets into slot
+// [rank] of every peer (16 B per row) and the last CTA raises the flags.
+// Reduce: once every source has signalled, lse = M + log(sum_r se_r exp(mx_r - M))
+// with M = max_r mx_r, and the target logit is the sum over ranks (only the
+// owner of the label's vocabulary row contributes a non-zero value).
+__global__ void __launch_bounds__(256) tp_ce_push_kernel(const float* __restrict__ mx, const float* __restrict__ se,
+                                                         const float* __restrict__ tg, int rows, const AgPush P) {
+  pdl_trigger();
+  pdl_wait();
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const float4 v = make_float4(mx[r], se[r], tg[r], 0.f);
+    for (int p = 0; p < P.world; ++p)
+      reinterpret_cast<float4*>(P.dst[p])[(long)P.rank * rows + r] = v;
+  }
+  grid_done_signal(P.flags, P.world, P.rank, P.epoch, P.counter);
+}
+
+__global__ void __launch_bounds__(256) tp_ce_reduce_kernel(const float4* __restrict__ slots, int rows, int world,
+                                                           const int* __restrict__ flags, int epoch,
+                                                           float* __restrict__ lse, float* __restrict__ tg,
+                                                           int* err, unsigned long long timeout_ns) {
+  pdl_trigger();
+  pdl_wait();
+  if (!cta_wait_flags(flags, world, epoch, err, timeout_ns)) return;
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    float m = -INFINITY;
+    for (int s = 0; s < world; ++s) m = fmaxf(m, slots[(long)s * rows + r].x);
+    float sum = 0.f, t = 0.f;
+    for (int s = 0; s < world; ++s) {
+      const float4 v = slots[(long)s * rows + r];
+      sum += v.y * __expf(v.x - m);
+      t += v.z;
+    }
+    lse[r] = m + logf(sum);
+    tg[r] = t;
+  }
+}
+
+int tp_ce_allreduce(const float* mx, const float* se, const float* tg_in, int rows, const AgPush& push,
+                    const void* slots_local, const int* flags_local, float* lse, float* tg_out, int* err, int num_sms,
+                    cudaStream_t s, unsigned long long timeout_ns) {
+  if (push.world < 1 || push.world > 8 || rows < 1) return -1;
+  const int blocks = std::max(1, std::min((rows + 255) / 256, num_sms));
+  launch_k(tp_ce_push_kernel, blocks, 256, 0, s, mx, se, tg_in, rows, push);
+  launch_k(tp_ce_reduce_kernel, blocks, 256, 0, s, reinterpret_cast<const float4*>(slots_local), rows, push.world,
+           flags_local, push.epoch, lse, tg_out, err, timeout_ns);
+  return (int)cudaGetLastError();
+}
+
 int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
                  const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
                  cudaStream_t s, unsigned long long timeout_ns) {

@@ -58,6 +58,19 @@ __device__ __forceinline__ void tile_coords(int t, int mtiles, int ntiles, int& 
   tn = r / gsz;
 }
 
+// Tile order of a GEMM.  For an all-gather consumer the 128-row tiles of each
+// sequence are rotated by this rank's shard (rank * Sl rows), so every rank
+// starts with the rows it produced itself (already local) while the peers'
+// shards are still arriving.
+__device__ __forceinline__ void gemm_tile(const GemmArgs& args, int t, int mtiles, int ntiles, int& tm, int& tn) {
+  tile_coords(t, mtiles, ntiles, tm, tn);
+  if (args.ag_flags != nullptr) {
+    const int tps = args.ag_S / BM;
+    const int b = tm / tps, k = tm % tps;
+    tm = b * tps + (k + args.ag_rank * (args.ag_Sl / BM)) % tps;
+  }
+}
+
 // ---------------------------------------------------------------- epilogue helpers
 // Each epilogue warp owns 32 accumulator rows (one per lane).  A chunk of its
 // rows is staged in shared memory as 32 rows x 128 bytes in the TMA 128-byte
@@ -176,7 +189,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t ag_ready = 0;  // source ranks whose rows are known to have arrived
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t / splits, mtiles, ntiles, tm, tn);
+        gemm_tile(args, t / splits, mtiles, ntiles, tm, tn);
         const int m0 = tm * BM, n0 = tn * BN;
         if (args.ag_flags != nullptr) {
           const int src = (m0 % args.ag_S) / args.ag_Sl;
@@ -306,7 +319,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint4 side[8];
     auto prefetch_side = [&](int tt, int ch) {
       int pm, pn;
-      tile_coords(tt / splits, mtiles, ntiles, pm, pn);
+      gemm_tile(args, tt / splits, mtiles, ntiles, pm, pn);
       const int pr0 = pm * BM + q * 32, pc0 = pn * BN + ch * W;
       side_prefetch(side, side_base + ((size_t)pr0 * side_ld + pc0) * SIDE_ES, side_ld * SIDE_ES,
                     min(32, args.M - pr0), (args.N - pc0) * SIDE_ES, lane);
@@ -315,7 +328,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // tile, else its first chunk of the next tile of this CTA (if any)
     auto prefetch_next_side = [&](int tt, int ch) {
       int nt = tt, nch = ch + 2, cm, cn;
-      tile_coords(tt / splits, mtiles, ntiles, cm, cn);
+      gemm_tile(args, tt / splits, mtiles, ntiles, cm, cn);
       if (nch >= BN / W || cn * BN + nch * W >= args.N) {
         nt = tt + gridDim.x;
         nch = half;
@@ -337,7 +350,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t / splits, mtiles, ntiles, tm, tn);
+      gemm_tile(args, t / splits, mtiles, ntiles, tm, tn);
       const int r0 = tm * BM + q * 32;                 // first row of this warp
       const int n0 = tn * BN;
       const int rows_valid = min(32, args.M - r0);

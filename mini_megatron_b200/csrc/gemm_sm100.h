@@ -35,6 +35,7 @@ struct GemmArgs {
   // loaded only after ag_flags[o] >= ag_epoch (nullptr: no waiting)
   const int* ag_flags;
   int ag_epoch, ag_S, ag_Sl;
+  int ag_rank;  // this rank: its own rows are computed first
   // reduce-scatter producer (EPI_PUSH_BF16): row m goes to owner o = (m % push_S) / push_Sl,
   // local row (m / push_S) * push_Sl + m % push_Sl of push_dst[o] (ld = ldd)
   void* push_dst[8];

@@ -41,6 +41,9 @@ int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mea
                        const float* gamma, const float* dres, float* dx, float* part, float* dgamma, float* dbeta,
                        int rows, int H, int nparts, const AgPush& push, cudaStream_t s);
 
+int tp_ce_allreduce(const float* mx, const float* se, const float* tg_in, int rows, const AgPush& push,
+                    const void* slots_local, const int* flags_local, float* lse, float* tg_out, int* err, int num_sms,
+                    cudaStream_t s, unsigned long long timeout_ns);
 int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
                  const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
                  cudaStream_t s,

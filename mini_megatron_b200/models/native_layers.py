@@ -17,10 +17,12 @@ autocast, main.py:93 + model/transformer.py:59-62).  GEMM operands are bf16,
 accumulation fp32.  Weight gradients never pass through autograd: the
 wgrad GEMMs accumulate into ``param.main_grad`` (see param_buffer.py).
 
-Tensor parallel collectives use NCCL through torch.distributed here (the
-fused NVLink kernels replace them when ``mmb_fused_tp`` is enabled on the
-model, see ops/fused_tp.py).  ``S_local = S / tp`` under sequence
-parallelism, ``S`` otherwise.
+Tensor-parallel collectives: with a ``TPWorkspace`` attached (``tp_impl``
+"fused", the default on CUDA with tp > 1; parallel/fused_tp.py) the decoder
+layers and the head run the sequence-parallel dataflow with every collective
+inside the kernels (NVLink pushes and flag waits); otherwise they go through
+NCCL via torch.distributed.  The embedding's TP reduction stays on NCCL in
+both cases.  ``S_local = S / tp`` under sequence parallelism, ``S`` otherwise.
 """
 from __future__ import annotations
 
@@ -297,14 +299,36 @@ class HeadLossFn(torch.autograd.Function):
         ctx.n_params = len(params)
         B, S_l, H = x.shape
         x2 = x.reshape(-1, H).contiguous()
-        ln, m, r = _ln_fwd(x2, ln_f)
-        ln_full = _gather_seq(ln, B, group) if sp else ln
         w = lm_head.weight
         V_local = w.shape[0]
         tp_rank = dist.get_rank(group=group) if _world(group) > 1 else 0
         vstart = tp_rank * V_local
         n_valid = max(0, min(V_local, n_vocab - vstart))
         lab = labels.reshape(-1).contiguous()
+        ws = getattr(lm_head, "_mmb_tp_ws", None) if sp else None
+        ctx.ws = ws
+        if ws is not None:
+            # fused TP: ln_f rows pushed to every rank, lm_head GEMM waiting per source rank, the
+            # cross-entropy statistics combined over NVLink (no NCCL collective in the head)
+            ln_full, m, r, e = ws.ln_fwd_ag(x2, ln_f, lm_head._mmb_tp_slot)
+            logits = torch.empty(ln_full.shape[0], V_local, device=x.device, dtype=torch.bfloat16)
+            mx, se, tg = ws.gemm_ce(ln_full, e, bf16_weight(w), logits, lab, vstart, n_valid)
+            if ws.copy_saved:
+                ln_full = ln_full.clone()
+            lse, tg = ws.ce_allreduce(mx, se, tg)
+            valid = (lab != -100).float()
+            mask = loss_mask.reshape(-1).float()
+            denom = mask.sum()
+            loss = ((lse - tg) * valid * mask).sum() / denom
+            ctx.save_for_backward(x2, m, r, ln_full, logits, lse, lab, valid * mask / denom)
+            ctx.ln_f, ctx.lm_head, ctx.group, ctx.sp, ctx.B, ctx.vstart, ctx.n_valid = (
+                ln_f, lm_head, group, sp, B, vstart, n_valid)
+            ctx.x_shape = x.shape
+            ctx.mark_non_differentiable(logits)
+            ctx.set_materialize_grads(False)
+            return loss, logits
+        ln, m, r = _ln_fwd(x2, ln_f)
+        ln_full = _gather_seq(ln, B, group) if sp else ln
         if _CE_FUSED:
             # the lm_head epilogue writes per-tile (max, sumexp) partials: no second pass over the logits
             logits = torch.empty(ln_full.shape[0], V_local, device=x.device, dtype=torch.bfloat16)
@@ -340,6 +364,19 @@ class HeadLossFn(torch.autograd.Function):
         scale = (wscale * dloss.float()).contiguous()
         native().ce_bwd(logits, lab, ctx.vstart, ctx.n_valid, lse.contiguous(), scale)   # logits -> dlogits
         w = ctx.lm_head.weight
+        ws = ctx.ws
+        if ws is not None:
+            # lm_head input gradient: partial tiles pushed to their owners, reduced there; ln_f backward
+            # pushes its bf16 rows to every rank for the last layer's gathered gradient
+            e_rs = ws.gemm_rs(logits, bf16_weight(w), True)
+            linear_wgrad(logits, ln_full, grad_target(w))
+            d_ln = ws.rs_reduce(e_rs, out_bf16=True)
+            dx = ws.ln_bwd_ag(d_ln, x2, m, r, ctx.ln_f, None, grad_target)
+            run_grad_ready_hooks(ctx.lm_head)
+            run_grad_ready_hooks(ctx.ln_f)
+            out = dx.view(ctx.x_shape)
+            out._mmb_gathered = dx._mmb_gathered
+            return (out, None, None, None, None, None, None, None) + (None,) * ctx.n_params
         d_ln = linear_dgrad(logits, bf16_weight(w))
         linear_wgrad(logits, ln_full, grad_target(w))
         if _world(ctx.group) > 1:

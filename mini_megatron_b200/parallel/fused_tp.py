@@ -13,7 +13,12 @@ the kernels around each collective do the communication themselves:
 * **GEMM -> reduce-scatter** (``gemm_tp`` with ``EPI_PUSH_BF16``): the Row GEMM's
   epilogue pushes each partial output tile into the owning rank's per-source
   slot; ``tp_rs_reduce`` waits for all sources and sums the slots plus the
-  residual.
+  residual;
+* **head**: ``ln_f`` pushes its rows like the layer LayerNorms, the lm_head GEMM
+  with the cross-entropy statistics epilogue waits per source rank, the
+  per-row (max, sum-exp, target) triplets of each vocabulary shard are pushed
+  to every rank and combined by ``tp_ce_allreduce``, and the lm_head input
+  gradient goes through the same reduce-scatter push as a Row GEMM.
 
 ``TPWorkspace`` owns the symmetric buffers of one model chunk: a signal pad
 (all-gather flags, reduce-scatter flags), two gathered buffers per decoder
@@ -35,7 +40,7 @@ from ..ops import native
 
 
 class TPWorkspace:
-    SIG_BYTES = 4096  # int32 flags: [0:8] all-gather, [8:16] reduce-scatter
+    SIG_BYTES = 4096  # int32 flags: [0:8] all-gather, [8:16] reduce-scatter, [16:24] cross-entropy statistics
 
     def __init__(self, tp_group, B: int, S: int, H: int, num_fwd_slots: int, copy_saved: bool = False):
         self.group = tp_group
@@ -53,7 +58,8 @@ class TPWorkspace:
         self.off_fwd = self.SIG_BYTES
         self.off_bwd = self.off_fwd + num_fwd_slots * slot_bytes
         self.off_rs = self.off_bwd + 2 * slot_bytes
-        total = self.off_rs + self.world * self.rows_l * H * 2
+        self.off_ce = self.off_rs + self.world * self.rows_l * H * 2   # [world][rows] float4 (mx, se, tg, -)
+        total = self.off_ce + self.world * self.rows * 16
         self.num_fwd_slots = num_fwd_slots
         self.slot_bytes = slot_bytes
         self.symm = SymmetricBuffer(total, tp_group)
@@ -61,8 +67,10 @@ class TPWorkspace:
         self.counters = torch.zeros(8, dtype=torch.int32, device=dev)
         self.ag_flag_ptrs = [self.symm.peer_ptr(r, 0) for r in range(self.world)]
         self.rs_flag_ptrs = [self.symm.peer_ptr(r, 32) for r in range(self.world)]
+        self.ce_flag_ptrs = [self.symm.peer_ptr(r, 64) for r in range(self.world)]
         self.ag_epoch = 0
         self.rs_epoch = 0
+        self.ce_epoch = 0
         self._bwd_next = 0
         dist.barrier(group=tp_group)
 
@@ -172,6 +180,19 @@ class TPWorkspace:
         out = torch.empty(self.rows_l, self.H, device=dev, dtype=torch.float32)
         C.tp_rs_reduce(self.rs_local_ptr, n, self.world, self.rs_flag_ptrs[self.rank], epoch, resid, out, None, n)
         return out
+
+    def gemm_ce(self, A_full, ag_epoch, W, logits, labels, vocab_start, n_valid):
+        """lm_head GEMM on the gathered rows (waiting per source rank) with cross-entropy statistics."""
+        return native().gemm_ce_stats(A_full, W, logits, labels, vocab_start, n_valid, self.ag_flag_ptrs[self.rank],
+                                      ag_epoch, self.S, self.Sl, self.rank)
+
+    def ce_allreduce(self, mx, se, tg):
+        """(lse, target logit) of every row over the whole vocabulary from each rank's shard statistics."""
+        self.ce_epoch += 1
+        dst = [self.symm.peer_ptr(r, self.off_ce) for r in range(self.world)]
+        return native().tp_ce_allreduce(mx.contiguous(), se.contiguous(), tg.contiguous(), dst, self.ce_flag_ptrs,
+                                        self.rank, self.ce_epoch, self.counters[4:5],
+                                        self.symm.peer_ptr(self.rank, self.off_ce), self.ce_flag_ptrs[self.rank])
 
     def close(self):
         if self.symm is not None:

@@ -176,10 +176,14 @@ class Trainer:
         if self.tp_impl == "fused":
             from .parallel.fused_tp import TPWorkspace
             self.tp_ws = TPWorkspace(mpu["tp_group"], cfg.micro_batch_size, self.seq_len, cfg.model.hidden_size,
-                                     num_fwd_slots=2 * len(layers), copy_saved=cfg.pp > 1)
+                                     num_fwd_slots=2 * len(layers) + 1, copy_saved=cfg.pp > 1)
             for i, layer in enumerate(layers):
                 layer._mmb_tp_ws = self.tp_ws
                 layer._mmb_tp_slot = i
+            head = getattr(self.model, "lm_head", None)
+            if head is not None:  # the last pipeline stage: ln_f / lm_head / cross-entropy collectives fused too
+                head._mmb_tp_ws = self.tp_ws
+                head._mmb_tp_slot = 2 * len(layers)
         # Modules whose native backward announces "gradients final".  DP buckets launch strictly in
         # order, head first, so the head and the embedding are attached as well: buckets then start
         # during backward (with MMB_DP_EARLY_BUCKETS=0 every bucket starts after backward).
