@@ -311,10 +311,33 @@ int layernorm_fwd(const float* x, const float* gamma, const float* beta, __nv_bf
 // above 48 KB in total the dynamic size must be opted in explicitly.
 constexpr int kLnStaticSmem = 256;
 
+// CTAs of the fused row pass that are resident at once: the row pass uses exactly that many
+// (one wave; a partial second wave of CTAs, each walking its rows in sequence, would leave
+// most SMs idle for its whole length).
+template <int NV>
+static int ln_bwd_resident(int H, int num_sms) {
+  static int cached_h = -1, n = 0;  // the occupancy depends on H through the shared-memory size
+  const int smem = 8 * 2 * (H / 4) * 16;
+  if (cached_h != H) {
+    cached_h = H;
+    if (smem + kLnStaticSmem > 48 * 1024)
+      cudaFuncSetAttribute(ln_bwd_kernel<NV, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, ln_bwd_kernel<NV, true>, 256, smem) != cudaSuccess || b < 1)
+      b = 1;
+    n = b;
+  }
+  return n * num_sms;
+}
+
 int layernorm_bwd_parts(int rows, int H, int num_sms) {
   const int nv = (H / 4 + 31) / 32;
-  if (nv <= 8) return std::min(4 * num_sms, std::max(1, (rows + 7) / 8));  // one per CTA of 8 warps
-  return std::min(4 * num_sms, std::max(1, rows / 16));                          // one per band
+  if (nv <= 8) {  // one partial row per CTA of 8 warps
+    const int resident = nv <= 2 ? ln_bwd_resident<2>(H, num_sms)
+                                 : (nv <= 6 ? ln_bwd_resident<6>(H, num_sms) : ln_bwd_resident<8>(H, num_sms));
+    return std::min(resident, std::max(1, (rows + 7) / 8));
+  }
+  return std::min(4 * num_sms, std::max(1, rows / 16));  // one per band
 }
 
 int layernorm_bwd(const __nv_bfloat16* dy, const float* x, const float* mean, const float* rstd, const float* gamma,

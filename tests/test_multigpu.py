@@ -236,7 +236,7 @@ def test_fused_tp_poisoned_workspace_gives_identical_results():
         assert poisoned[r]["losses"][0] == clean[r]["losses"][0]           # first forward: no reductions differ
         for a, b in zip(poisoned[r]["losses"], clean[r]["losses"]):
             assert abs(a - b) <= 1e-4 * abs(b), (poisoned[r]["losses"], clean[r]["losses"])
-        _assert_states_close(poisoned[r]["state"], clean[r]["state"])
+        _assert_states_close(poisoned[r]["state"], clean[r]["state"], tensor_rel=1e-2)
 
 
 @NEED2
