@@ -34,6 +34,33 @@ from ..ops import native
 from .param_buffer import ParamBuffer
 
 
+def replication_runs(offsets, kinds, numel, shards, max_segs):
+    """Replication runs of each owned shard, in float4 units relative to the shard start.
+
+    ``offsets[i]`` / ``kinds[i]``: flat start and kind of parameter i (in buffer order);
+    kind 0 = GEMM weight (the kernels read its bf16 shadow: only that is all-gathered), kind 1 =
+    LayerNorm / embedding / 1-D parameter (its kernels read fp32).  The padding after a
+    parameter belongs to that parameter's run; adjacent runs of one kind merge.  Returns, per
+    ``(lo, hi)`` in ``shards``, a list of ``[begin4, end4, kind, 0]`` covering ``[lo, hi)``, or
+    None when it would need more than ``max_segs`` runs (the kernel then all-gathers every
+    element in both precisions).
+    """
+    out = []
+    for lo, hi in shards:
+        runs = []
+        for i, (off, kind) in enumerate(zip(offsets, kinds)):
+            end = offsets[i + 1] if i + 1 < len(offsets) else numel
+            a, z = max(off, lo), min(end, hi)
+            if a >= z:
+                continue
+            if runs and runs[-1][2] == kind and runs[-1][1] == (a - lo) // 4:
+                runs[-1][1] = (z - lo) // 4
+            else:
+                runs.append([(a - lo) // 4, (z - lo) // 4, kind, 0])
+        out.append(runs if runs and len(runs) <= max_segs else None)
+    return out
+
+
 class FusedDPOptimizer(torch.optim.Optimizer):
     def __init__(self, module: torch.nn.Module, dp_group, lr=6e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01,
                  bucket_elems=16 << 20, overlap=True, max_ctas=64, defer_done=False, tail_ctas=None):
@@ -104,38 +131,15 @@ class FusedDPOptimizer(torch.optim.Optimizer):
             dist.barrier(group=dp_group)
 
     def _replication_runs(self, module):
-        """Per bucket: int32 [nseg, 4] runs {begin4, end4, kind, 0} of this rank's owned range.
-
-        kind 0: a GEMM weight -- the kernels read its bf16 shadow, so only that is all-gathered;
-        kind 1: LayerNorm / embedding parameters and 1-D tensors -- their kernels read fp32.
-        Padding after a parameter belongs to that parameter's run.  A bucket with more runs than
-        the kernel stages gets None (every element is then all-gathered in both precisions).
-        """
+        """Per bucket: int32 [nseg, 4] runs {begin4, end4, kind, 0} of this rank's owned range (or None)."""
         from .tensor_parallel import VocabParallelEmbedding
         fp32_ids = set()
         for m in module.modules():
             if isinstance(m, (torch.nn.LayerNorm, torch.nn.Embedding, VocabParallelEmbedding)):
                 fp32_ids.update(id(p) for p in m.parameters(recurse=False))
-        kind_of = {id(p): (1 if (id(p) in fp32_ids or p.dim() != 2) else 0) for p in self.buf.params}
-        starts = [(off, kind_of[id(p)]) for p, off in zip(self.buf.params, self.buf.offsets)]
-        max_segs = native().dp_max_segments()
-        out = []
-        for b, (lo, hi) in enumerate(self.shards):
-            runs = []
-            for i, (off, kind) in enumerate(starts):
-                end = starts[i + 1][0] if i + 1 < len(starts) else self.buf.numel
-                a, z = max(off, lo), min(end, hi)
-                if a >= z:
-                    continue
-                if runs and runs[-1][2] == kind and runs[-1][1] == (a - lo) // 4:
-                    runs[-1][1] = (z - lo) // 4
-                else:
-                    runs.append([(a - lo) // 4, (z - lo) // 4, kind, 0])
-            if not runs or len(runs) > max_segs:
-                out.append(None)
-            else:
-                out.append(torch.tensor(runs, dtype=torch.int32).to(self.buf.data.device))
-        return out
+        kinds = [1 if (id(p) in fp32_ids or p.dim() != 2) else 0 for p in self.buf.params]
+        runs = replication_runs(self.buf.offsets, kinds, self.buf.numel, self.shards, native().dp_max_segments())
+        return [None if r is None else torch.tensor(r, dtype=torch.int32).to(self.buf.data.device) for r in runs]
 
     @torch.no_grad()
     def gather_master(self):
