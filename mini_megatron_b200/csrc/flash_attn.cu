@@ -739,8 +739,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
 // delta[b, h, pos] = sum_d dO[row, h*D + d] * O[row, h*D + d]
 // One thread per 8 elements (16 bytes); the D/8 threads of a (row, head) reduce with shuffles.
+// The same thread also zeroes the 8 matching fp32 elements of the dQ accumulator (same
+// [B*S, nh*D] layout), which the backward then fills with bulk reduce-adds.
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
-                                  long ld, int B, int S, int nh, int D, float* __restrict__ delta) {
+                                  long ld, int B, int S, int nh, int D, float* __restrict__ delta,
+                                  float* __restrict__ dq_zero) {
   pdl_trigger();
   pdl_wait();
   const int g = D / 8;  // threads per (row, head): 8 or 16
@@ -756,6 +759,11 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const 
     h = (int)(pair % nh);
     const uint4 x = *reinterpret_cast<const uint4*>(dout + row * ld + h * D + part * 8);
     const uint4 y = *reinterpret_cast<const uint4*>(out + row * ld + h * D + part * 8);
+    if (dq_zero) {
+      float4* z = reinterpret_cast<float4*>(dq_zero + row * ld + h * D + part * 8);
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x);
     const uint32_t* yw = reinterpret_cast<const uint32_t*>(&y);
 #pragma unroll
@@ -800,9 +808,9 @@ int flash_attn_bwd(const __nv_bfloat16* dout, long ld_do, const __nv_bfloat16* q
   // Delta = rowsum(dO * O)
   {
     const long threads = rows * nh * (d / 8);
-    launch_k(attn_delta_kernel, (unsigned)((threads + 255) / 256), 256, 0, stream, dout, out, ld_do, B, S, nh, d, delta);
+    launch_k(attn_delta_kernel, (unsigned)((threads + 255) / 256), 256, 0, stream, dout, out, ld_do, B, S, nh, d, delta,
+             dq_acc);
   }
-  cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * nh * d, stream);
   const long n4 = rows * nh * d / 4;
   if (d == 64 && !one_tile_per_cta) {
     // persistent key/value-stationary kernel (flash_bwd_sm100.cu)

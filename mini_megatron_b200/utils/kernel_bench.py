@@ -62,9 +62,14 @@ def bench_gemm(args):
         Bt = B if b_mn else B.t()
         lib = _timeit(lambda: torch.matmul(At, Bt, out=D), flush=flush)
         flops = 2.0 * M * N * K
-        print(json.dumps({"kernel": "gemm_bf16_sm100", "name": name, "M": M, "N": N, "K": K,
-                          "ms": round(ours, 4), "tflops": round(flops / ours / 1e9, 1),
-                          "cublas_ms": round(lib, 4), "cublas_tflops": round(flops / lib / 1e9, 1)}))
+        rec = {"kernel": "gemm_bf16_sm100", "name": name, "M": M, "N": N, "K": K,
+               "ms": round(ours, 4), "tflops": round(flops / ours / 1e9, 1),
+               "cublas_ms": round(lib, 4), "cublas_tflops": round(flops / lib / 1e9, 1)}
+        if args.tile_widths:  # the same GEMM with each output tile width forced
+            for bn in (128, 256):
+                t = _timeit(lambda: _C.gemm(A, a_mn, B, b_mn, D, _C.EPI_BF16, bn=bn), flush=flush)
+                rec[f"bn{bn}_ms"] = round(t, 4)
+        print(json.dumps(rec), flush=True)
     assert _C.get_error() == 0
 
 
@@ -200,6 +205,7 @@ def main():
     ap.add_argument("--model", default="gpt-125m")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--d", type=int, default=64)
+    ap.add_argument("--tile-widths", action="store_true", help="gemm: also time 128- and 256-wide output tiles")
     args = ap.parse_args()
     {"gemm": bench_gemm, "profile": profile_case, "attn": bench_attn, "attn_case": attn_case}[args.kernel](args)
 
