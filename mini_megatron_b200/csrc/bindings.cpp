@@ -563,6 +563,78 @@ std::vector<Tensor> tp_ce_allreduce(const Tensor& mx, const Tensor& se, const Te
   return {lse, tgo};
 }
 
+// ---- embedding and sequence-parallel gradients under fused TP (NVLink, no NCCL)
+void tp_emb_fwd_push(const Tensor& ids, const Tensor& tok, const Tensor& pos, const std::vector<int64_t>& dst,
+                     const std::vector<int64_t>& flags, int64_t rank, int64_t epoch, int64_t S, int64_t Sl,
+                     Tensor& counter, int64_t vstart, int64_t vend) {
+  check_f32(tok, "tok");
+  check_f32(pos, "pos");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.is_cuda(), "ids: contiguous CUDA int64");
+  const int H = (int)tok.size(1);
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, S, Sl, H, counter);
+  MMB_CHECK_RC(mmb::tp_emb_fwd_push(ids.data_ptr<int64_t>(), tok.data_ptr<float>(), pos.data_ptr<float>(),
+                                    (int)ids.numel(), H, vstart, vend, P, num_sms(), cur_stream()),
+               "tp_emb_fwd_push");
+}
+
+void tp_wait_copy(int64_t src, Tensor& dst, int64_t add, int64_t flags, int64_t world, int64_t epoch,
+                  int64_t timeout_ms) {
+  check_f32(dst, "dst");
+  MMB_CHECK_RC(mmb::tp_wait_copy(reinterpret_cast<const float*>(src), dst.data_ptr<float>(), dst.numel(), (int)add,
+                                 reinterpret_cast<const int*>(flags), (int)world, (int)epoch, error_word(), num_sms(),
+                                 cur_stream(), (unsigned long long)timeout_ms * 1000000ull),
+               "tp_wait_copy");
+}
+
+void tp_publish(const Tensor& src, const std::vector<int64_t>& dst, const std::vector<int64_t>& flags, int64_t rank,
+                int64_t epoch, Tensor& counter) {
+  check_f32(src, "src");
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, 1, 1, 4, counter);
+  MMB_CHECK_RC(mmb::tp_publish(src.data_ptr<float>(), src.numel(), P, num_sms(), cur_stream()), "tp_publish");
+}
+
+void tp_pos_grad_push(const Tensor& dout, int64_t B, const std::vector<int64_t>& dst,
+                      const std::vector<int64_t>& flags, int64_t rank, int64_t epoch, int64_t S, int64_t Sl,
+                      Tensor& counter) {
+  check_f32(dout, "dout");
+  const int H = (int)dout.size(-1);
+  TORCH_CHECK(dout.numel() == B * Sl * H, "tp_pos_grad_push: dout must be [B*Sl, H]");
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, S, Sl, H, counter);
+  MMB_CHECK_RC(mmb::tp_pos_grad_push(dout.data_ptr<float>(), (int)B, H, P, num_sms(), cur_stream()),
+               "tp_pos_grad_push");
+}
+
+void tp_vec_allreduce(const Tensor& v, Tensor& out, const std::vector<int64_t>& dst,
+                      const std::vector<int64_t>& flags, int64_t rank, int64_t epoch, Tensor& counter,
+                      int64_t slots_local, int64_t flags_local, int64_t timeout_ms) {
+  check_f32(v, "v");
+  check_f32(out, "out");
+  TORCH_CHECK(v.numel() == out.numel(), "tp_vec_allreduce: sizes");
+  mmb::AgPush P = make_push(dst, flags, rank, epoch, 1, 1, 1, counter);
+  MMB_CHECK_RC(mmb::tp_vec_allreduce(v.data_ptr<float>(), out.data_ptr<float>(), v.numel(), P,
+                                     reinterpret_cast<const float*>(slots_local),
+                                     reinterpret_cast<const int*>(flags_local), error_word(), num_sms(), cur_stream(),
+                                     (unsigned long long)timeout_ms * 1000000ull),
+               "tp_vec_allreduce");
+}
+
+void embedding_bwd_peers(const Tensor& ids, const std::vector<int64_t>& src, int64_t flags_local, int64_t epoch,
+                         int64_t S, int64_t Sl, Tensor& dwte, int64_t vstart, int64_t vend) {
+  check_f32(dwte, "dwte");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous() && ids.is_cuda(), "ids: contiguous CUDA int64");
+  TORCH_CHECK(src.size() >= 1 && src.size() <= 8, "embedding_bwd_peers: 1..8 ranks");
+  mmb::EmbPeers P{};
+  for (size_t i = 0; i < src.size(); ++i) P.src[i] = reinterpret_cast<const float*>(src[i]);
+  P.flags = reinterpret_cast<const int*>(flags_local);
+  P.world = (int)src.size();
+  P.epoch = (int)epoch;
+  P.S = (int)S;
+  P.Sl = (int)Sl;
+  MMB_CHECK_RC(mmb::embedding_bwd_peers(ids.data_ptr<int64_t>(), P, dwte.data_ptr<float>(), (int)ids.numel(),
+                                        (int)dwte.size(1), vstart, vend, error_word(), cur_stream()),
+               "embedding_bwd_peers");
+}
+
 // lm_head GEMM whose epilogue also writes per-tile cross-entropy partials, then the
 // merge: returns (max, sumexp, target logit) per row like ce_fwd_stats.
 // With ag_flags != 0 the rows of A are a sequence-parallel all-gather in progress: the GEMM's
@@ -734,6 +806,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ce_stats", &gemm_ce_stats, "lm_head GEMM with cross-entropy statistics fused into its epilogue",
         py::arg("A"), py::arg("B"), py::arg("D"), py::arg("labels"), py::arg("vocab_start"), py::arg("n_valid"),
         py::arg("ag_flags") = 0, py::arg("ag_epoch") = 0, py::arg("S") = 0, py::arg("Sl") = 0, py::arg("rank") = 0);
+  m.def("tp_emb_fwd_push", &tp_emb_fwd_push);
+  m.def("tp_wait_copy", &tp_wait_copy, py::arg("src"), py::arg("dst"), py::arg("add"), py::arg("flags"),
+        py::arg("world"), py::arg("epoch"), py::arg("timeout_ms") = 10000);
+  m.def("tp_publish", &tp_publish);
+  m.def("tp_pos_grad_push", &tp_pos_grad_push);
+  m.def("tp_vec_allreduce", &tp_vec_allreduce, py::arg("v"), py::arg("out"), py::arg("dst"), py::arg("flags"),
+        py::arg("rank"), py::arg("epoch"), py::arg("counter"), py::arg("slots_local"), py::arg("flags_local"),
+        py::arg("timeout_ms") = 10000);
+  m.def("embedding_bwd_peers", &embedding_bwd_peers);
   m.def("tp_ce_allreduce", &tp_ce_allreduce, py::arg("mx"), py::arg("se"), py::arg("tg"), py::arg("dst"),
         py::arg("flags"), py::arg("rank"), py::arg("epoch"), py::arg("counter"), py::arg("slots_local"),
         py::arg("flags_local"), py::arg("timeout_ms") = 10000);

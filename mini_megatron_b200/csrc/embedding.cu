@@ -11,6 +11,7 @@
 //           the main grads.
 #include "common.cuh"
 #include "ops.h"
+#include "peer.cuh"
 
 #include <algorithm>
 
@@ -54,12 +55,28 @@ __global__ void emb_fwd_kernel(const long* __restrict__ ids, const float* __rest
 constexpr int kEmbList = 4096;
 constexpr int kEmbThreads = 256;
 
+// PEERS: the gradient rows are spread over the TP ranks by sequence shard (row p of the full
+// [B*S, H] gradient is local row (p / S) * Sl + p % S - o * Sl of rank o = (p % S) / Sl) and
+// read from there over NVLink once every rank has published its rows.
+template <bool PEERS>
 __global__ void __launch_bounds__(kEmbThreads) emb_bwd_tok_kernel(const long* __restrict__ ids,
                                                                   const float* __restrict__ dout,
                                                                   float* __restrict__ dwte, int rows, int H,
-                                                                  long vstart, long vend, int rows_per_cta) {
+                                                                  long vstart, long vend, int rows_per_cta,
+                                                                  const EmbPeers peers, int* err) {
   pdl_trigger();
   pdl_wait();
+  if constexpr (PEERS) {
+    if (!cta_wait_flags(peers.flags, peers.world, peers.epoch, err)) return;
+  }
+  auto grad_row = [&](int p) -> const float* {
+    if constexpr (PEERS) {
+      const int s = p % peers.S, o = s / peers.Sl;
+      return peers.src[o] + ((size_t)(p / peers.S) * peers.Sl + (s - o * peers.Sl)) * H;
+    } else {
+      return dout + (size_t)p * H;
+    }
+  };
   __shared__ int list_pos[kEmbList];
   __shared__ int list_row[kEmbList];
   __shared__ int warp_tot[kEmbThreads / 32];
@@ -124,7 +141,7 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_tok_kernel(const long* __
           while (m2) {
             const int k = __ffs(m2) - 1;
             m2 &= m2 - 1;
-            const float4 d = reinterpret_cast<const float4*>(dout + (size_t)list_pos[b + k] * H)[c];
+            const float4 d = reinterpret_cast<const float4*>(grad_row(list_pos[b + k]))[c];
             acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
           }
           wrow[c] = acc;
@@ -163,8 +180,23 @@ int embedding_bwd(const long* ids, const float* dout, float* dwte, float* dwpe, 
   const long vrows = vend - vstart;
   const int grid = (int)std::max<long>(1, std::min<long>(2L * sms, (vrows + 63) / 64));
   const int rows_per_cta = (int)((vrows + grid - 1) / grid);
-  launch_k(emb_bwd_tok_kernel, grid, kEmbThreads, 0, s, ids, dout, dwte, rows, H, vstart, vend, rows_per_cta);
+  launch_k(emb_bwd_tok_kernel<false>, grid, kEmbThreads, 0, s, ids, dout, dwte, rows, H, vstart, vend, rows_per_cta,
+           EmbPeers{}, (int*)nullptr);
   if (dwpe) launch_k(emb_bwd_pos_kernel, S, 256, 0, s, dout, dwpe, B, S, H);
+  return (int)cudaGetLastError();
+}
+
+int embedding_bwd_peers(const long* ids, const EmbPeers& peers, float* dwte, int rows, int H, long vstart, long vend,
+                        int* err, cudaStream_t s) {
+  if (H % 4 || peers.world < 1 || peers.world > 8 || peers.Sl <= 0 || peers.S % peers.Sl) return -1;
+  int dev = 0, sms = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long vrows = vend - vstart;
+  const int grid = (int)std::max<long>(1, std::min<long>(2L * sms, (vrows + 63) / 64));
+  const int rows_per_cta = (int)((vrows + grid - 1) / grid);
+  launch_k(emb_bwd_tok_kernel<true>, grid, kEmbThreads, 0, s, ids, (const float*)nullptr, dwte, rows, H, vstart, vend,
+           rows_per_cta, peers, err);
   return (int)cudaGetLastError();
 }
 

@@ -44,6 +44,22 @@ int layernorm_bwd_push(const __nv_bfloat16* dy, const float* x, const float* mea
 int tp_ce_allreduce(const float* mx, const float* se, const float* tg_in, int rows, const AgPush& push,
                     const void* slots_local, const int* flags_local, float* lse, float* tg_out, int* err, int num_sms,
                     cudaStream_t s, unsigned long long timeout_ns);
+int tp_emb_fwd_push(const long* ids, const float* tok, const float* pos, int rows, int H, long vstart, long vend,
+                    const AgPush& push, int num_sms, cudaStream_t s);
+int tp_wait_copy(const float* src, float* dst, long n, int add, const int* flags, int world, int epoch, int* err,
+                 int num_sms, cudaStream_t s, unsigned long long timeout_ns);
+int tp_publish(const float* src, long n, const AgPush& push, int num_sms, cudaStream_t s);
+int tp_pos_grad_push(const float* dout, int B, int H, const AgPush& push, int num_sms, cudaStream_t s);
+int tp_vec_allreduce(const float* v, float* out, long n, const AgPush& push, const float* slots_local,
+                     const int* flags_local, int* err, int num_sms, cudaStream_t s, unsigned long long timeout_ns);
+// token-table gradient reading the gradient rows of other ranks' sequence shards (fused TP)
+struct EmbPeers {
+  const float* src[8];   // each rank's published [B*Sl, H] gradient rows
+  const int* flags;      // this rank's flags, one per source rank
+  int world, epoch, S, Sl;
+};
+int embedding_bwd_peers(const long* ids, const EmbPeers& peers, float* dwte, int rows, int H, long vstart, long vend,
+                        int* err, cudaStream_t s);
 int tp_rs_reduce(const __nv_bfloat16* slots, long slot_stride, int world, const int* flags, int epoch,
                  const float* resid, float* out, __nv_bfloat16* out_bf16, long n, int* err, int num_sms,
                  cudaStream_t s,

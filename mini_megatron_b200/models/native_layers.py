@@ -19,10 +19,10 @@ wgrad GEMMs accumulate into ``param.main_grad`` (see param_buffer.py).
 
 Tensor-parallel collectives: with a ``TPWorkspace`` attached (``tp_impl``
 "fused", the default on CUDA with tp > 1; parallel/fused_tp.py) the decoder
-layers and the head run the sequence-parallel dataflow with every collective
-inside the kernels (NVLink pushes and flag waits); otherwise they go through
-NCCL via torch.distributed.  The embedding's TP reduction stays on NCCL in
-both cases.  ``S_local = S / tp`` under sequence parallelism, ``S`` otherwise.
+layers, the head and the embedding run the sequence-parallel dataflow with
+every collective inside the kernels (NVLink pushes and flag waits); otherwise
+they go through NCCL via torch.distributed.  ``S_local = S / tp`` under
+sequence parallelism, ``S`` otherwise.
 """
 from __future__ import annotations
 
@@ -264,6 +264,15 @@ class EmbeddingFn(torch.autograd.Function):
         B, S = ids.shape
         H = tok.weight.shape[1]
         ids_c = ids.contiguous()
+        ws = getattr(emb, "_mmb_tp_ws", None) if sp else None
+        ctx.ws = ws
+        if ws is not None:
+            # fused TP: each vocabulary owner writes tok + pos of its rows into their sequence owner
+            out = ws.emb_fwd(ids_c.view(-1), tok.weight.detach(), emb.position_embedding.weight.detach(),
+                             tok.vocab_start_index, tok.vocab_end_index)
+            ctx.save_for_backward(ids_c)
+            ctx.emb, ctx.group, ctx.sp = emb, group, sp
+            return out.view(B, -1, H)
         full = torch.empty(B * S, H, device=ids.device, dtype=torch.float32)
         tp_rank = dist.get_rank(group=group) if _world(group) > 1 else 0
         wpe = emb.position_embedding.weight.detach() if tp_rank == 0 else None
@@ -282,6 +291,12 @@ class EmbeddingFn(torch.autograd.Function):
         B, S = ids.shape
         H = dout.shape[-1]
         d2 = dout.reshape(-1, H).contiguous().float()
+        if ctx.ws is not None:
+            ctx.ws.emb_bwd(ids.view(-1), d2, grad_target(tok.weight),
+                           grad_target(pos.weight) if pos.weight.requires_grad else None,
+                           tok.vocab_start_index, tok.vocab_end_index)
+            run_grad_ready_hooks(emb)
+            return (None, None, None, None) + (None,) * ctx.n_params
         if ctx.sp:
             d2 = _gather_seq(d2, B, group).contiguous()
         native().embedding_bwd(ids.view(-1), d2, grad_target(tok.weight),

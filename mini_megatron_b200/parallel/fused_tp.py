@@ -40,9 +40,12 @@ from ..ops import native
 
 
 class TPWorkspace:
-    SIG_BYTES = 4096  # int32 flags: [0:8] all-gather, [8:16] reduce-scatter, [16:24] cross-entropy statistics
+    # int32 flags: [0:8] all-gather, [8:16] reduce-scatter, [16:24] cross-entropy statistics, [24:32] embedding
+    # rows, [32:40] published embedding gradients, [40:48] position-table gradient, [48:56] small-vector sums
+    SIG_BYTES = 4096
 
-    def __init__(self, tp_group, B: int, S: int, H: int, num_fwd_slots: int, copy_saved: bool = False):
+    def __init__(self, tp_group, B: int, S: int, H: int, num_fwd_slots: int, copy_saved: bool = False,
+                 vec_elems: int = 0):
         self.group = tp_group
         self.world = dist.get_world_size(tp_group)
         self.rank = dist.get_rank(tp_group)
@@ -59,18 +62,28 @@ class TPWorkspace:
         self.off_bwd = self.off_fwd + num_fwd_slots * slot_bytes
         self.off_rs = self.off_bwd + 2 * slot_bytes
         self.off_ce = self.off_rs + self.world * self.rows_l * H * 2   # [world][rows] float4 (mx, se, tg, -)
-        total = self.off_ce + self.world * self.rows * 16
+        self.off_embo = self.off_ce + self.world * self.rows * 16      # [rows_l, H] fp32 embedding rows (pushed in)
+        self.off_embd = self.off_embo + self.rows_l * H * 4            # [rows_l, H] fp32 embedding gradient (published)
+        self.off_posg = self.off_embd + self.rows_l * H * 4            # [S, H] fp32 position-table gradient
+        self.off_vec = self.off_posg + S * H * 4                       # [world][vec_elems] fp32
+        self.vec_elems = vec_elems
+        total = self.off_vec + self.world * max(vec_elems, 1) * 4
         self.num_fwd_slots = num_fwd_slots
         self.slot_bytes = slot_bytes
         self.symm = SymmetricBuffer(total, tp_group)
         dev = self.symm.device
-        self.counters = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.counters = torch.zeros(16, dtype=torch.int32, device=dev)
         self.ag_flag_ptrs = [self.symm.peer_ptr(r, 0) for r in range(self.world)]
         self.rs_flag_ptrs = [self.symm.peer_ptr(r, 32) for r in range(self.world)]
         self.ce_flag_ptrs = [self.symm.peer_ptr(r, 64) for r in range(self.world)]
+        self.emb_flag_ptrs = [self.symm.peer_ptr(r, 96) for r in range(self.world)]
+        self.pub_flag_ptrs = [self.symm.peer_ptr(r, 128) for r in range(self.world)]
+        self.pos_flag_ptrs = [self.symm.peer_ptr(r, 160) for r in range(self.world)]
+        self.vec_flag_ptrs = [self.symm.peer_ptr(r, 192) for r in range(self.world)]
         self.ag_epoch = 0
         self.rs_epoch = 0
         self.ce_epoch = 0
+        self.emb_epoch = self.pub_epoch = self.pos_epoch = self.vec_epoch = 0
         self._bwd_next = 0
         dist.barrier(group=tp_group)
 
@@ -193,6 +206,53 @@ class TPWorkspace:
         return native().tp_ce_allreduce(mx.contiguous(), se.contiguous(), tg.contiguous(), dst, self.ce_flag_ptrs,
                                         self.rank, self.ce_epoch, self.counters[4:5],
                                         self.symm.peer_ptr(self.rank, self.off_ce), self.ce_flag_ptrs[self.rank])
+
+    def _ptrs(self, off):
+        return [self.symm.peer_ptr(r, off) for r in range(self.world)]
+
+    def emb_fwd(self, ids, tok_w, pos_w, vstart, vend):
+        """Embedding of this rank's sequence shard: every vocabulary owner writes tok + pos of the
+        rows whose token it holds into the rows' sequence owner (no reduction: one writer per row)."""
+        C = native()
+        self.emb_epoch += 1
+        C.tp_emb_fwd_push(ids, tok_w, pos_w, self._ptrs(self.off_embo), self.emb_flag_ptrs, self.rank,
+                          self.emb_epoch, self.S, self.Sl, self.counters[5:6], vstart, vend)
+        out = torch.empty(self.rows_l, self.H, device=self.symm.device, dtype=torch.float32)
+        C.tp_wait_copy(self.symm.peer_ptr(self.rank, self.off_embo), out, 0, self.emb_flag_ptrs[self.rank],
+                       self.world, self.emb_epoch)
+        return out
+
+    def emb_bwd(self, ids, d_local, tok_grad, pos_grad, vstart, vend):
+        """Token-table gradient from every rank's gradient rows (read over NVLink by the row owner),
+        and the full position-table gradient on every rank (each rank pushes its shard's rows)."""
+        C = native()
+        self.pub_epoch += 1
+        C.tp_publish(d_local, self._ptrs(self.off_embd), self.pub_flag_ptrs, self.rank, self.pub_epoch,
+                     self.counters[6:7])
+        C.embedding_bwd_peers(ids, self._ptrs(self.off_embd), self.pub_flag_ptrs[self.rank], self.pub_epoch, self.S,
+                              self.Sl, tok_grad, vstart, vend)
+        if pos_grad is not None:
+            self.pos_epoch += 1
+            C.tp_pos_grad_push(d_local, self.B, self._ptrs(self.off_posg), self.pos_flag_ptrs, self.rank,
+                               self.pos_epoch, self.S, self.Sl, self.counters[7:8])
+            C.tp_wait_copy(self.symm.peer_ptr(self.rank, self.off_posg), pos_grad[:self.S], 1,
+                           self.pos_flag_ptrs[self.rank], self.world, self.pos_epoch)
+
+    def vec_allreduce(self, grads):
+        """In-place sum over the TP group of a few small fp32 tensors (sequence-parallel LayerNorm grads)."""
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        if flat.numel() > self.vec_elems:
+            raise ValueError("TP workspace sized for fewer vector elements")
+        self.vec_epoch += 1
+        out = torch.empty_like(flat)
+        native().tp_vec_allreduce(flat, out, self._ptrs(self.off_vec), self.vec_flag_ptrs, self.rank, self.vec_epoch,
+                                  self.counters[8:9], self.symm.peer_ptr(self.rank, self.off_vec),
+                                  self.vec_flag_ptrs[self.rank])
+        off = 0
+        for g in grads:
+            n = g.numel()
+            g.copy_(out[off:off + n].view_as(g))
+            off += n
 
     def close(self):
         if self.symm is not None:

@@ -175,8 +175,9 @@ class Trainer:
         self.tp_ws = None
         if self.tp_impl == "fused":
             from .parallel.fused_tp import TPWorkspace
+            sp_elems = sum(p.numel() for p in self.model.parameters() if getattr(p, "sequence_parallel_grad", False))
             self.tp_ws = TPWorkspace(mpu["tp_group"], cfg.micro_batch_size, self.seq_len, cfg.model.hidden_size,
-                                     num_fwd_slots=2 * len(layers) + 1, copy_saved=cfg.pp > 1)
+                                     num_fwd_slots=2 * len(layers) + 1, copy_saved=cfg.pp > 1, vec_elems=sp_elems)
             for i, layer in enumerate(layers):
                 layer._mmb_tp_ws = self.tp_ws
                 layer._mmb_tp_slot = i
@@ -184,6 +185,9 @@ class Trainer:
             if head is not None:  # the last pipeline stage: ln_f / lm_head / cross-entropy collectives fused too
                 head._mmb_tp_ws = self.tp_ws
                 head._mmb_tp_slot = 2 * len(layers)
+            emb = getattr(self.model, "embedding", None)
+            if emb is not None:  # the first pipeline stage: the embedding's TP exchange over NVLink too
+                emb._mmb_tp_ws = self.tp_ws
         # Modules whose native backward announces "gradients final".  DP buckets launch strictly in
         # order, head first, so the head and the embedding are attached as well: buckets then start
         # during backward (with MMB_DP_EARLY_BUCKETS=0 every bucket starts after backward).
@@ -371,7 +375,10 @@ class Trainer:
             if not cfg.zero1 and self.dp_impl != "fused":
                 self.grad_sync.finish()
             if self.sp_params:
-                allreduce_sequence_parallel_grads(self.sp_params, self.mpu["tp_group"])
+                if self.tp_ws is not None:   # fused TP: summed over NVLink
+                    self.tp_ws.vec_allreduce([grad_of(p) for p in self.sp_params])
+                else:
+                    allreduce_sequence_parallel_grads(self.sp_params, self.mpu["tp_group"])
             self.optimizer.step()
             self.scheduler.step()
         self.step_count += 1
@@ -392,6 +399,12 @@ class Trainer:
         if hasattr(self.optimizer, "close"):
             self.optimizer.close()
         pg.set_model_parallel(None)
+
+
+def grad_of(p):
+    """The gradient a native kernel accumulated for ``p`` (main_grad when managed, else .grad)."""
+    g = getattr(p, "main_grad", None)
+    return g if g is not None else p.grad
 
 
 def synthetic_batch(num_microbatches, B, S, vocab, seed=0, pin=False, shift=True):
