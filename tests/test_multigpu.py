@@ -315,3 +315,17 @@ def test_fused_dp_composes_with_tp_and_pp(tp, pp):
             if b is not None:
                 assert abs(a - b) < 1e-3 * abs(b), (fused[r]["losses"], nccl[r]["losses"])
         _assert_states_close(fused[r]["state"], nccl[r]["state"], tensor_rel=1e-2, model_rel=1e-3)
+
+
+@NEED4
+def test_fused_tp_with_pp_matches_nccl_tp():
+    """TP2 x PP2: the first stage holds the embedding (rows written by their vocabulary owner,
+    gradient rows read back over NVLink), the last stage the fused head; both must reproduce the
+    NCCL sequence-parallel path of the same configuration."""
+    fused = _run(_train, 4, 2, 2, True, "nccl", 3, 4, "fused", port=29741)
+    nccl = _run(_train, 4, 2, 2, True, "nccl", 3, 4, "nccl", port=29742)
+    for r in range(4):
+        for a, b in zip(fused[r]["losses"], nccl[r]["losses"]):
+            if b is not None:
+                assert abs(a - b) < 2e-3 * abs(b), (fused[r]["losses"], nccl[r]["losses"])
+        _assert_states_close(fused[r]["state"], nccl[r]["state"], tensor_rel=1e-2, model_rel=1e-3)
