@@ -56,7 +56,8 @@ void set_error(int64_t code) {
 
 // ----------------------------------------------------------------- GEMM
 void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, Tensor& D, int64_t epi,
-          const c10::optional<Tensor>& aux, const c10::optional<Tensor>& resid, double alpha, int64_t bn) {
+          const c10::optional<Tensor>& aux, const c10::optional<Tensor>& resid, double alpha, int64_t bn,
+          int64_t cg) {
   check_cuda(A, "A");
   check_cuda(B, "B");
   check_cuda(D, "D");
@@ -85,6 +86,7 @@ void gemm(const Tensor& A, bool a_mn, const Tensor& B, bool b_mn, Tensor& D, int
   p.N = (int)N;
   p.K = (int)K;
   p.bn = (int)bn;
+  p.cg = (int)cg;
   p.num_sms = num_sms();
   p.allow_split = true;
   p.args.epi = (int)epi;
@@ -797,7 +799,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_error", &set_error, "write the device error word from the host (tests of the host-side check)");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM with fused epilogue", py::arg("A"), py::arg("a_mn"), py::arg("B"),
         py::arg("b_mn"), py::arg("D"), py::arg("epi"), py::arg("aux") = c10::nullopt,
-        py::arg("resid") = c10::nullopt, py::arg("alpha") = 1.0, py::arg("bn") = 0);
+        py::arg("resid") = c10::nullopt, py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("cg") = 0);
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
         py::arg("gamma"), py::arg("dres"), py::arg("dx"), py::arg("dgamma"), py::arg("dbeta"),

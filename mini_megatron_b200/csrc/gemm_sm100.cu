@@ -16,10 +16,18 @@
 // model: GELU (fc1), GELU-backward (fc2 dgrad), residual add (attn.o / fc2),
 // and fp32 gradient accumulation into the flat main-grad buffer (wgrad).
 //
-// CTA = 6 warps: warp 0 issues TMA loads, warp 1 owns TMEM and issues
-// tcgen05.mma from one thread, warps 2-5 drain the accumulator (tcgen05.ld)
+// CTA = 10 warps: warp 0 issues TMA loads, warp 1 owns TMEM and issues
+// tcgen05.mma from one thread, warps 2-9 drain the accumulator (tcgen05.ld)
 // and run the epilogue.  Two TMEM accumulators let the epilogue of tile i
-// overlap the main loop of tile i+1.  Tiles are 128 x BN x 64.
+// overlap the main loop of tile i+1.  Tiles are 128 x BN x 64 per CTA.
+//
+// CTA pairs (CG = 2): a 2-CTA cluster on one TPC computes a 256 x 256 tile.
+// Each CTA TMA-loads its own 128 rows of A and 128 of the 256 B rows (no tile is
+// copied between the two CTAs), with the transaction bytes completing on the even
+// CTA's barrier; that CTA alone issues tcgen05.mma.cta_group::2, which reads both
+// CTAs' shared memory and writes each CTA's 128 x 256 accumulator into its own
+// TMEM.  Per SM, a 64-deep k-block then moves 32 KB of operands instead of 48 KB
+// for the same MMA work.
 #include "common.cuh"
 #include "gemm_sm100.h"
 #include "peer.cuh"
@@ -35,11 +43,14 @@ constexpr int BK = 64;
 constexpr int kGemmThreads = 320;  // 2 producer/MMA warps + 8 epilogue warps
 constexpr int kEpiWarps = 8;
 
-template <int BN>
+// CG = CTAs per output tile: 1, or 2 for a CTA pair (2-CTA cluster) that computes a
+// 256 x BN tile with pair MMAs, each CTA holding 128 rows of A and BN/2 rows of B.
+template <int BN, int CG = 1>
 struct GemmCfg {
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs use 256-wide tiles");
+  static constexpr int STAGES = (BN == 256 && CG == 1) ? 4 : 6;
   static constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-  static constexpr int B_BYTES = BN * BK * 2;          // 32 KB / 16 KB
+  static constexpr int B_BYTES = (BN / CG) * BK * 2;   // 32 KB / 16 KB (this CTA's share)
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;             // double-buffered accumulator
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 8 * 4096 /*epilogue*/ + 256;  // one 4 KB stage per epilogue warp
@@ -62,12 +73,30 @@ __device__ __forceinline__ void tile_coords(int t, int mtiles, int ntiles, int& 
 // sequence are rotated by this rank's shard (rank * Sl rows), so every rank
 // starts with the rows it produced itself (already local) while the peers'
 // shards are still arriving.
+__device__ __forceinline__ int ag_rotate(const GemmArgs& args, int tm) {
+  const int tps = args.ag_S / BM;
+  const int b = tm / tps, k = tm % tps;
+  return b * tps + (k + args.ag_rank * (args.ag_Sl / BM)) % tps;
+}
 __device__ __forceinline__ void gemm_tile(const GemmArgs& args, int t, int mtiles, int ntiles, int& tm, int& tn) {
   tile_coords(t, mtiles, ntiles, tm, tn);
-  if (args.ag_flags != nullptr) {
-    const int tps = args.ag_S / BM;
-    const int b = tm / tps, k = tm % tps;
-    tm = b * tps + (k + args.ag_rank * (args.ag_Sl / BM)) % tps;
+  if (args.ag_flags != nullptr) tm = ag_rotate(args, tm);
+}
+
+// This CTA's 128-row m-tile and BN-wide n-tile of work unit u (u / splits is the
+// output tile; for a CTA pair, the output tile is a pair of m-tiles 2p, 2p + 1 that
+// share one n-tile, and CTA `crank` of the pair takes m-tile 2p + crank).  The
+// rotation of an all-gather consumer is applied per 128-row m-tile: the pair MMA
+// needs the two CTAs to share B, not to hold adjacent rows of A.
+template <int CG>
+__device__ __forceinline__ void unit_tile(const GemmArgs& args, int u, int splits, int mtiles, int ntiles, int crank,
+                                          int& tm, int& tn) {
+  if constexpr (CG == 1) {
+    gemm_tile(args, u / splits, mtiles, ntiles, tm, tn);
+  } else {
+    tile_coords(u / splits, (mtiles + 1) >> 1, ntiles, tm, tn);
+    tm = 2 * tm + crank;
+    if (args.ag_flags != nullptr && tm < mtiles) tm = ag_rotate(args, tm);
   }
 }
 
@@ -119,13 +148,13 @@ __device__ __forceinline__ void side_to_stage(uint8_t* stg, const uint4 (&buf)[8
   for (int it = 0; it < 8; ++it) *reinterpret_cast<uint4*>(stage_unit(stg, it * 4 + (lane >> 3), unit)) = buf[it];
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmAux,
                     const GemmArgs args) {
   pdl_trigger();
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, CG>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -144,6 +173,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // CTA pair: rank 0 (leader) owns the stage-full and accumulator-empty barriers
+  // and issues the MMAs; both CTAs load their own operand halves and drain their
+  // own accumulator rows.
+  const uint32_t crank = (CG == 2) ? cluster_ctarank() : 0u;
+  const bool leader = (crank == 0);
+  const int u0 = blockIdx.x / CG;      // first work unit of this CTA (pair)
+  const int ustep = gridDim.x / CG;    // CTAs (pairs) in the persistent grid
+  // a failed wait in one CTA of a pair also stops the other one
+  auto raise_abort = [&]() {
+    *abort_flag = 1;
+    if constexpr (CG == 2) st_cluster_u32(cluster_addr((const void*)abort_flag, crank ^ 1u), 1u);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -152,7 +193,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 32 * kEpiWarps);
+      // 1 CTA: every epilogue thread arrives; pair: one arrival per epilogue warp of both CTAs
+      mbar_init(&acc_empty[b], CG == 1 ? 32 * kEpiWarps : 2 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -162,11 +204,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     prefetch_tmap(&tmD);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 1) {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    } else {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 1) {
+    __syncthreads();
+  } else {
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // set-up above touched no global memory; everything below may depend on the previous kernel
@@ -177,7 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Work unit = (output tile, K split).  Splits > 1 only with the atomic epilogue.
   const int splits = args.splits > 0 ? args.splits : 1;
   const int kb_per_split = (kblocks_total + splits - 1) / splits;
-  const int num_tiles = mtiles * ntiles * splits;
+  const int num_tiles = (CG == 1 ? mtiles : (mtiles + 1) >> 1) * ntiles * splits;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -187,15 +238,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued_mask = 0, issued_par = 0;
       bool ok = true;
       uint32_t ag_ready = 0;  // source ranks whose rows are known to have arrived
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = u0; t < num_tiles && ok; t += ustep) {
         int tm, tn;
-        gemm_tile(args, t / splits, mtiles, ntiles, tm, tn);
-        const int m0 = tm * BM, n0 = tn * BN;
-        if (args.ag_flags != nullptr) {
+        unit_tile<CG>(args, t, splits, mtiles, ntiles, (int)crank, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN + (int)crank * (BN / CG);
+        if (args.ag_flags != nullptr && tm < mtiles) {
           const int src = (m0 % args.ag_S) / args.ag_Sl;
           if (!((ag_ready >> src) & 1u)) {
             if (!wait_flag_ge(args.ag_flags + src, args.ag_epoch, args.err)) {
-              *abort_flag = 1;
+              raise_abort();
               ok = false;
               break;
             }
@@ -206,26 +257,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int kb_hi = min(kblocks_total, kb_lo + kb_per_split);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrGemmEmptyWait, abort_flag)) {
+            raise_abort();
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-          issued_mask |= 1u << stage;
-          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           uint8_t* a_dst = sA + stage * C::A_BYTES;
           uint8_t* b_dst = sB + stage * C::B_BYTES;
           const int k0 = kb * BK;
-          if constexpr (!A_MN) {
-            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
-          } else {
+          if constexpr (CG == 1) {
+            mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+            issued_mask |= 1u << stage;
+            issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+            if constexpr (!A_MN) {
+              tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
-          }
-          if constexpr (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
-          } else {
+              for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], m0 + 64 * j, k0);
+            }
+            if constexpr (!B_MN) {
+              tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+            }
+          } else {
+            // both CTAs' bytes complete on the leader's barrier, which expects them all
+            if (leader) {
+              mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+              issued_mask |= 1u << stage;
+              issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+            }
+            const uint32_t fb = cluster_addr(&full[stage], 0);
+            if constexpr (!A_MN) {
+              tma_load_2d_pair(a_dst, &tmA, fb, k0, m0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * 8192, &tmA, fb, m0 + 64 * j, k0);
+            }
+            if constexpr (!B_MN) {
+              tma_load_2d_pair(b_dst, &tmB, fb, k0, n0);
+            } else {
+#pragma unroll
+              for (int j = 0; j < (BN / CG) / 64; ++j) tma_load_2d_pair(b_dst + j * 8192, &tmB, fb, n0 + 64 * j, k0);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -236,6 +310,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!ok) {
         // Let loads already in flight land before the CTA (and its smem) goes
         // away: stage s completes the phase with the parity it was issued in.
+        // (A pair's follower has no barrier of its own to watch; the closing
+        // cluster barrier keeps it alive until the leader has drained.)
         for (int s = 0; s < STAGES; ++s) {
           if (!((issued_mask >> s) & 1u)) continue;
           const uint32_t par = (issued_par >> s) & 1u;
@@ -246,17 +322,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+    // ------------------------------------------------------------ MMA issuer (pair: leader only)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM * CG, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = u0; t < num_tiles && ok; t += ustep, ++it) {
         const int buf = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, args.err, kErrGemmAccEmptyWait, abort_flag)) {
+          raise_abort();
           ok = false;
           break;
         }
@@ -266,6 +343,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int kb_hi = min(kblocks_total, kb_lo + kb_per_split);
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[stage], phase, args.err, kErrGemmFullWait, abort_flag)) {
+            raise_abort();
             ok = false;
             break;
           }
@@ -278,20 +356,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                         : make_sdesc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_sdesc_sw128(b_addr + k * 2048, 8192, 1024)
                                         : make_sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
+            if constexpr (CG == 1)
+              umma_bf16_ss(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
+            else
+              umma_bf16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);  // frees the smem stage once these MMAs have read it
+          // frees the smem stage (of both CTAs) once these MMAs have read it
+          if constexpr (CG == 1) {
+            umma_commit(&empty[stage]);
+          } else {
+            umma_commit_pair(cluster_addr(&empty[stage], 0));
+            umma_commit_pair(cluster_addr(&empty[stage], 1));
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&acc_full[buf]);   // accumulator ready for the epilogue
+        // accumulator ready for the epilogue(s)
+        if constexpr (CG == 1) {
+          umma_commit(&acc_full[buf]);
+        } else {
+          umma_commit_pair(cluster_addr(&acc_full[buf], 0));
+          umma_commit_pair(cluster_addr(&acc_full[buf], 1));
+        }
       }
       if (!ok) {
         // Drain: wait (bounded) until every MMA issued so far has completed.
-        umma_commit(drain);
+        if constexpr (CG == 1)
+          umma_commit(drain);
+        else
+          umma_commit_pair(cluster_addr(drain, 0));
         const unsigned long long t0 = globaltimer();
         while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < 10000000ull) {
         }
@@ -319,7 +415,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint4 side[8];
     auto prefetch_side = [&](int tt, int ch) {
       int pm, pn;
-      gemm_tile(args, tt / splits, mtiles, ntiles, pm, pn);
+      unit_tile<CG>(args, tt, splits, mtiles, ntiles, (int)crank, pm, pn);
       const int pr0 = pm * BM + q * 32, pc0 = pn * BN + ch * W;
       side_prefetch(side, side_base + ((size_t)pr0 * side_ld + pc0) * SIDE_ES, side_ld * SIDE_ES,
                     min(32, args.M - pr0), (args.N - pc0) * SIDE_ES, lane);
@@ -328,18 +424,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // tile, else its first chunk of the next tile of this CTA (if any)
     auto prefetch_next_side = [&](int tt, int ch) {
       int nt = tt, nch = ch + 2, cm, cn;
-      gemm_tile(args, tt / splits, mtiles, ntiles, cm, cn);
+      unit_tile<CG>(args, tt, splits, mtiles, ntiles, (int)crank, cm, cn);
       if (nch >= BN / W || cn * BN + nch * W >= args.N) {
-        nt = tt + gridDim.x;
+        nt = tt + ustep;
         nch = half;
       }
       if (nt < num_tiles) prefetch_side(nt, nch);
     };
     if constexpr (SIDE) {
-      if (blockIdx.x < num_tiles) prefetch_side(blockIdx.x, half);
+      if (u0 < num_tiles) prefetch_side(u0, half);
     }
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int t = u0; t < num_tiles; t += ustep, ++it) {
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       // One lane waits, the warp follows: tcgen05.ld below is warp-collective,
@@ -347,10 +443,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&acc_full[buf], acc_phase, args.err, kErrGemmAccFullWait, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (!ok) {
+        if (lane == 0) raise_abort();
+        break;
+      }
       tc_fence_after();
       int tm, tn;
-      gemm_tile(args, t / splits, mtiles, ntiles, tm, tn);
+      unit_tile<CG>(args, t, splits, mtiles, ntiles, (int)crank, tm, tn);
       const int r0 = tm * BM + q * 32;                 // first row of this warp
       const int n0 = tn * BN;
       const int rows_valid = min(32, args.M - r0);
@@ -527,14 +626,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           args.ce_part[(size_t)(r0 + lane) * args.ce_ld + 2 * tn + half] = make_float2(ce_m, ce_s);
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      if constexpr (CG == 1) {
+        mbar_arrive(&acc_empty[buf]);
+      } else {
+        __syncwarp();  // the whole warp's TMEM reads are done
+        if (lane == 0) mbar_arrive_remote(cluster_addr(&acc_empty[buf], 0));
+      }
     }
     if (lane == 0) bulk_wait<0>();
     __syncwarp();
   }
 
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 1) {
+    __syncthreads();
+  } else {
+    // neither CTA of a pair leaves while the other may still signal its barriers,
+    // read its shared memory or write its tensor memory
+    cluster_sync_all();
+  }
   if constexpr (EPI == EPI_PUSH_BF16) {
     // every tile of this rank has been pushed: the last CTA tells each owner
     if (!*abort_flag)
@@ -542,7 +652,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (CG == 1)
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -591,46 +704,92 @@ int make_tmap_f32_2d(CUtensorMap* map, const void* base, long rows, long cols, l
   return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_cols, box_rows);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+// Launch of one instantiation.  `grid` is in CTAs (even for CTA pairs); pairs are
+// launched as 2-CTA clusters, capped at the number of clusters that fit at once.
+template <int BN, bool A_MN, bool B_MN, int EPI, int CG>
 static cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                               const CUtensorMap& tx, const GemmArgs& args, int grid, cudaStream_t stream) {
-  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI>;
-  constexpr int smem = GemmCfg<BN>::SMEM_BYTES;
+  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI, CG>;
+  constexpr int smem = GemmCfg<BN, CG>::SMEM_BYTES;
   static bool attr_set = false;  // per instantiation
+  static int max_pairs = 0;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
+    if constexpr (CG == 2) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(2 * 74);
+      q.blockDim = dim3(kGemmThreads);
+      q.dynamicSmemBytes = smem;
+      cudaLaunchAttribute ca[1];
+      ca[0].id = cudaLaunchAttributeClusterDimension;
+      ca[0].val.clusterDim.x = 2;
+      ca[0].val.clusterDim.y = 1;
+      ca[0].val.clusterDim.z = 1;
+      q.attrs = ca;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        return cudaErrorInvalidConfiguration;
+      }
+      max_pairs = n;
+    }
     attr_set = true;
   }
-  launch_k(kern, grid, kGemmThreads, smem, stream, ta, tb, td, tx, args);
+  if constexpr (CG == 1) {
+    launch_k(kern, grid, kGemmThreads, smem, stream, ta, tb, td, tx, args);
+  } else {
+    const int pairs = std::max(1, std::min(grid / 2, max_pairs));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    int na = 1;
+    if (pdl_enabled()) {
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      na = 2;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, td, tx, args);
+    if (e != cudaSuccess) return e;
+  }
   return cudaGetLastError();
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int CG>
 static cudaError_t dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                                 const CUtensorMap& tx, const GemmArgs& args, int grid, cudaStream_t s) {
   switch (args.epi) {
-    case EPI_BF16: return launch_one<BN, A_MN, B_MN, EPI_BF16>(ta, tb, td, tx, args, grid, s);
-    case EPI_F32: return launch_one<BN, A_MN, B_MN, EPI_F32>(ta, tb, td, tx, args, grid, s);
-    case EPI_F32_ACC: return launch_one<BN, A_MN, B_MN, EPI_F32_ACC>(ta, tb, td, tx, args, grid, s);
-    case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU>(ta, tb, td, tx, args, grid, s);
-    case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID>(ta, tb, td, tx, args, grid, s);
-    case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU>(ta, tb, td, tx, args, grid, s);
-    case EPI_CE_STATS: return launch_one<BN, A_MN, B_MN, EPI_CE_STATS>(ta, tb, td, tx, args, grid, s);
-    case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC>(ta, tb, td, tx, args, grid, s);
-    case EPI_PUSH_BF16: return launch_one<BN, A_MN, B_MN, EPI_PUSH_BF16>(ta, tb, td, tx, args, grid, s);
+    case EPI_BF16: return launch_one<BN, A_MN, B_MN, EPI_BF16, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_F32: return launch_one<BN, A_MN, B_MN, EPI_F32, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_F32_ACC: return launch_one<BN, A_MN, B_MN, EPI_F32_ACC, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_GELU: return launch_one<BN, A_MN, B_MN, EPI_GELU, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_RESID: return launch_one<BN, A_MN, B_MN, EPI_RESID, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_DGELU: return launch_one<BN, A_MN, B_MN, EPI_DGELU, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_CE_STATS: return launch_one<BN, A_MN, B_MN, EPI_CE_STATS, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_F32_ATOMIC: return launch_one<BN, A_MN, B_MN, EPI_F32_ATOMIC, CG>(ta, tb, td, tx, args, grid, s);
+    case EPI_PUSH_BF16: return launch_one<BN, A_MN, B_MN, EPI_PUSH_BF16, CG>(ta, tb, td, tx, args, grid, s);
   }
   return cudaErrorInvalidValue;
 }
 
-template <int BN>
+template <int BN, int CG>
 static cudaError_t dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                                   const CUtensorMap& tx, const GemmArgs& args, bool a_mn, bool b_mn, int grid,
                                   cudaStream_t s) {
-  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false>(ta, tb, td, tx, args, grid, s);
-  if (!a_mn && b_mn) return dispatch_epi<BN, false, true>(ta, tb, td, tx, args, grid, s);
-  if (a_mn && b_mn) return dispatch_epi<BN, true, true>(ta, tb, td, tx, args, grid, s);
-  return dispatch_epi<BN, true, false>(ta, tb, td, tx, args, grid, s);
+  if (!a_mn && !b_mn) return dispatch_epi<BN, false, false, CG>(ta, tb, td, tx, args, grid, s);
+  if (!a_mn && b_mn) return dispatch_epi<BN, false, true, CG>(ta, tb, td, tx, args, grid, s);
+  if (a_mn && b_mn) return dispatch_epi<BN, true, true, CG>(ta, tb, td, tx, args, grid, s);
+  return dispatch_epi<BN, true, false, CG>(ta, tb, td, tx, args, grid, s);
 }
 
 int choose_bn(int M, int N, int num_sms) {
@@ -682,21 +841,37 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   args.splits = 1;
   int bn = p.bn > 0 ? p.bn : choose_bn(p.M, p.N, sms);
   const bool can_split = (args.epi == EPI_F32_ACC || args.epi == EPI_F32_ATOMIC) && p.allow_split;
+  // CTA pairs (256 x 256 output tiles over two SMs) for 256-wide tiles with at
+  // least two m-tiles.  Default: pairs unless K >= 32768 (the vocabulary-long
+  // K of the lm_head input gradient, measured slower with pairs on B200).
+  const int want_cg = p.cg > 0 ? p.cg : gemm_pairs_default(p.K);
+  int cg = (want_cg == 2 && p.M > BM && sms >= 2) ? 2 : 1;
   if (can_split) {
     int sbn = bn, sp = 1;
-    choose_split(p.M, p.N, p.K, sms, sbn, sp);
+    if (cg == 2) {
+      // pair units: ceil(M / 256) x n-tiles over sms / 2 pairs (same cost model, in pairs)
+      choose_split((int)(((p.M + 2 * BM - 1) / (2 * BM)) * BM), p.N, p.K, sms / 2, sbn, sp);
+      if ((p.bn > 0 ? p.bn : sbn) != 256) cg = 1;
+    }
+    if (cg == 1) {
+      sbn = bn;
+      sp = 1;
+      choose_split(p.M, p.N, p.K, sms, sbn, sp);
+    }
     if (p.bn <= 0) bn = sbn;
     if (sp > 1) {
       args.splits = sp;
       args.epi = EPI_F32_ATOMIC;
     }
   }
+  if (bn != 256) cg = 1;
   CUtensorMap ta, tb;
   int rc;
   if (!p.a_mn) rc = make_tmap_bf16_2d(&ta, p.A, p.M, p.K, p.lda, 64, BM);
   else rc = make_tmap_bf16_2d(&ta, p.A, p.K, p.M, p.lda, 64, 64);
   if (rc) return rc - 20;
-  if (!p.b_mn) rc = make_tmap_bf16_2d(&tb, p.B, p.N, p.K, p.ldb, 64, bn);
+  // K-major B: each CTA of a pair loads its bn / 2 rows
+  if (!p.b_mn) rc = make_tmap_bf16_2d(&tb, p.B, p.N, p.K, p.ldb, 64, bn / cg);
   else rc = make_tmap_bf16_2d(&tb, p.B, p.K, p.N, p.ldb, 64, 64);
   if (rc) return rc - 30;
   // output (and GELU pre-activation) maps for the TMA-store epilogue
@@ -721,11 +896,30 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   } else {
     tx = td;
   }
-  const long units = (long)((p.M + BM - 1) / BM) * ((p.N + bn - 1) / bn) * args.splits;
-  const int grid = (int)std::min<long>(units, sms);
-  cudaError_t e = (bn == 256) ? dispatch_major<256>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream)
-                              : dispatch_major<128>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream);
+  const long mt = (p.M + BM - 1) / BM;
+  const long units = (cg == 2 ? (mt + 1) / 2 : mt) * ((p.N + bn - 1) / bn) * args.splits;
+  cudaError_t e;
+  if (cg == 2) {
+    const int grid = 2 * (int)std::min<long>(units, sms / 2);
+    e = dispatch_major<256, 2>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream);
+  } else {
+    const int grid = (int)std::min<long>(units, sms);
+    e = (bn == 256) ? dispatch_major<256, 1>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream)
+                    : dispatch_major<128, 1>(ta, tb, td, tx, args, p.a_mn, p.b_mn, grid, stream);
+  }
   return e == cudaSuccess ? 0 : (int)e;
+}
+
+// Default for GemmProblem::cg == 0.  MMB_GEMM_PAIRS=0: single-CTA tiles only;
+// MMB_GEMM_PAIRS=1: pairs wherever eligible; unset: pairs for K < 32768.
+int gemm_pairs_default(int K) {
+  static const int mode = [] {
+    const char* e = getenv("MMB_GEMM_PAIRS");
+    if (e == nullptr || e[0] == 0) return -1;
+    return e[0] == '1' ? 1 : 0;
+  }();
+  if (mode >= 0) return mode == 1 ? 2 : 1;
+  return K < 32768 ? 2 : 1;
 }
 
 }  // namespace mmb

@@ -59,6 +59,7 @@ struct GemmProblem {
   int bn;       // 0 = heuristic, else 128 / 256
   int num_sms;  // persistent grid size cap
   bool allow_split;  // accumulate epilogues may split K across CTAs (atomics)
+  int cg;            // CTAs per output tile: 0 = default, 1 = one CTA (128 x bn), 2 = a CTA pair (256 x 256)
   GemmArgs args;
 };
 
@@ -67,5 +68,6 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, 
 int make_tmap_f32_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
 int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream);
 int choose_bn(int M, int N, int num_sms);
+int gemm_pairs_default(int K);
 
 }  // namespace mmb

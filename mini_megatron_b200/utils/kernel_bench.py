@@ -2,7 +2,7 @@
 
 Usage::
 
-    python -m mini_megatron_b200.utils.kernel_bench gemm [--model gpt-125m] [--tokens 16384]
+    python -m mini_megatron_b200.utils.kernel_bench gemm [--model gpt-125m] [--tokens 16384] [--pairs]
     python -m mini_megatron_b200.utils.kernel_bench attn      # causal attention vs torch SDPA
     python -m mini_megatron_b200.utils.kernel_bench attn_case --d 64   # one fwd + bwd launch (ncu target)
 
@@ -67,8 +67,16 @@ def bench_gemm(args):
                "cublas_ms": round(lib, 4), "cublas_tflops": round(flops / lib / 1e9, 1)}
         if args.tile_widths:  # the same GEMM with each output tile width forced
             for bn in (128, 256):
-                t = _timeit(lambda: _C.gemm(A, a_mn, B, b_mn, D, _C.EPI_BF16, bn=bn), flush=flush)
+                t = _timeit(lambda: _C.gemm(A, a_mn, B, b_mn, D, _C.EPI_BF16, bn=bn, cg=1), flush=flush)
                 rec[f"bn{bn}_ms"] = round(t, 4)
+        if args.pairs:  # one CTA per 128 x 256 tile against a CTA pair per 256 x 256 tile
+            D1 = torch.empty_like(D)
+            t1 = _timeit(lambda: _C.gemm(A, a_mn, B, b_mn, D1, _C.EPI_BF16, bn=256, cg=1), flush=flush)
+            t2 = _timeit(lambda: _C.gemm(A, a_mn, B, b_mn, D, _C.EPI_BF16, bn=256, cg=2), flush=flush)
+            torch.cuda.synchronize()
+            rec["cta1_ms"], rec["pair_ms"] = round(t1, 4), round(t2, 4)
+            rec["pair_tflops"] = round(flops / t2 / 1e9, 1)
+            rec["pair_vs_cta1_max_abs_diff"] = float((D.float() - D1.float()).abs().max())
         print(json.dumps(rec), flush=True)
     assert _C.get_error() == 0
 
@@ -206,6 +214,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--d", type=int, default=64)
     ap.add_argument("--tile-widths", action="store_true", help="gemm: also time 128- and 256-wide output tiles")
+    ap.add_argument("--pairs", action="store_true",
+                    help="gemm: also time one CTA per 128x256 tile against a CTA pair per 256x256 tile")
     args = ap.parse_args()
     {"gemm": bench_gemm, "profile": profile_case, "attn": bench_attn, "attn_case": attn_case}[args.kernel](args)
 

@@ -128,3 +128,59 @@ def test_gemm_side_input_epilogues_ragged(M, N):
     torch.cuda.synchronize()
     _check_close(R, expect, 1e-3)
     _check_close(D2, ref * gp.float(), 1e-2)
+
+
+# ----------------------------------------------------------------------------- CTA pairs
+# cg=2: a 2-CTA cluster computes a 256 x 256 output tile with pair MMAs, each CTA
+# holding 128 rows of A and 128 rows of B.  An odd number of 128-row m-tiles
+# leaves the second CTA of the last pair outside the matrix.
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (296, 392, 200), (384, 512, 320), (1024, 2304, 768)])
+def test_gemm_cta_pair_layouts(a_mn, b_mn, M, N, K):
+    C = _C()
+    A, B, ref = _operands(M, N, K, a_mn, b_mn, seed=21)
+    D = torch.full((M, N), float("nan"), device="cuda")
+    C.gemm(A, a_mn, B, b_mn, D, C.EPI_F32, bn=256, cg=2)
+    torch.cuda.synchronize()
+    assert C.get_error() == 0
+    _check_close(D, ref, 1e-3)
+
+
+def test_gemm_cta_pair_epilogues():
+    C = _C()
+    M, N, K = 8232, 832, 256          # 65 m-tiles, 4 n-tiles: several tiles per pair, ragged edges
+    A, B, ref = _operands(M, N, K, False, False, seed=22)
+    D = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, False, B, False, D, C.EPI_BF16, alpha=0.5, bn=256, cg=2)
+    gp = torch.empty_like(D)
+    act = torch.empty_like(D)
+    C.gemm(A, False, B, False, act, C.EPI_GELU, aux=gp, bn=256, cg=2)
+    R = torch.randn(M, N, device="cuda")
+    expect = R + ref
+    C.gemm(A, False, B, False, R, C.EPI_RESID, resid=R, bn=256, cg=2)
+    D2 = torch.empty_like(D)
+    C.gemm(A, False, B, False, D2, C.EPI_DGELU, aux=gp, bn=256, cg=2)
+    torch.cuda.synchronize()
+    assert C.get_error() == 0
+    _check_close(D, 0.5 * ref, 1e-2)
+    x = ref.clone().requires_grad_(True)
+    y = torch.nn.functional.gelu(x)
+    y.backward(torch.ones_like(y))
+    _check_close(act, y.detach(), 1e-2)
+    _check_close(gp, x.grad, 1e-2)
+    _check_close(R, expect, 1e-3)
+    _check_close(D2, ref * gp.float(), 1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(768, 768, 16384), (384, 2304, 4096)])
+def test_gemm_cta_pair_split_k_accumulate(M, N, K):
+    """Weight-gradient shapes: few output tiles, long K -> K splits with the atomic epilogue."""
+    C = _C()
+    A, B, ref = _operands(M, N, K, True, True, seed=23)
+    D = torch.randn(M, N, device="cuda")
+    D0 = D.clone()
+    C.gemm(A, True, B, True, D, C.EPI_F32_ACC, cg=2)
+    torch.cuda.synchronize()
+    assert C.get_error() == 0
+    _check_close(D, D0 + ref, 1e-3)
