@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 namespace mmb {
@@ -844,7 +845,7 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   // CTA pairs (256 x 256 output tiles over two SMs) for 256-wide tiles with at
   // least two m-tiles.  Default: pairs unless K >= 32768 (the vocabulary-long
   // K of the lm_head input gradient, measured slower with pairs on B200).
-  const int want_cg = p.cg > 0 ? p.cg : gemm_pairs_default(p.K);
+  const int want_cg = p.cg > 0 ? p.cg : gemm_pairs_default(p.K, p.args.epi);
   int cg = (want_cg == 2 && p.M > BM && sms >= 2) ? 2 : 1;
   if (can_split) {
     int sbn = bn, sp = 1;
@@ -911,15 +912,20 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
 }
 
 // Default for GemmProblem::cg == 0.  MMB_GEMM_PAIRS=0: single-CTA tiles only;
-// MMB_GEMM_PAIRS=1: pairs wherever eligible; unset: pairs for K < 32768.
-int gemm_pairs_default(int K) {
+// MMB_GEMM_PAIRS=1: pairs wherever eligible; unset: pairs for K < 32768 and the
+// epilogues in MMB_GEMM_PAIR_EPI_MASK (bit e = GemmEpilogue e; default all).
+int gemm_pairs_default(int K, int epi) {
   static const int mode = [] {
     const char* e = getenv("MMB_GEMM_PAIRS");
     if (e == nullptr || e[0] == 0) return -1;
     return e[0] == '1' ? 1 : 0;
   }();
+  static const unsigned mask = [] {
+    const char* e = getenv("MMB_GEMM_PAIR_EPI_MASK");
+    return (e != nullptr && e[0] != 0) ? (unsigned)strtoul(e, nullptr, 0) : 0x1FFu;
+  }();
   if (mode >= 0) return mode == 1 ? 2 : 1;
-  return K < 32768 ? 2 : 1;
+  return (K < 32768 && ((mask >> epi) & 1u)) ? 2 : 1;
 }
 
 }  // namespace mmb

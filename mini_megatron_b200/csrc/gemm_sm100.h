@@ -68,6 +68,6 @@ int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, 
 int make_tmap_f32_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols, int box_rows);
 int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream);
 int choose_bn(int M, int N, int num_sms);
-int gemm_pairs_default(int K);
+int gemm_pairs_default(int K, int epi);
 
 }  // namespace mmb
