@@ -843,8 +843,7 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
   int bn = p.bn > 0 ? p.bn : choose_bn(p.M, p.N, sms);
   const bool can_split = (args.epi == EPI_F32_ACC || args.epi == EPI_F32_ATOMIC) && p.allow_split;
   // CTA pairs (256 x 256 output tiles over two SMs) for 256-wide tiles with at
-  // least two m-tiles.  Default: pairs unless K >= 32768 (the vocabulary-long
-  // K of the lm_head input gradient, measured slower with pairs on B200).
+  // least two m-tiles; the default is in gemm_pairs_default.
   const int want_cg = p.cg > 0 ? p.cg : gemm_pairs_default(p.K, p.args.epi);
   int cg = (want_cg == 2 && p.M > BM && sms >= 2) ? 2 : 1;
   if (can_split) {
@@ -912,8 +911,16 @@ int gemm_bf16_launch(const GemmProblem& p, cudaStream_t stream) {
 }
 
 // Default for GemmProblem::cg == 0.  MMB_GEMM_PAIRS=0: single-CTA tiles only;
-// MMB_GEMM_PAIRS=1: pairs wherever eligible; unset: pairs for K < 32768 and the
-// epilogues in MMB_GEMM_PAIR_EPI_MASK (bit e = GemmEpilogue e; default all).
+// MMB_GEMM_PAIRS=1: pairs wherever eligible.  Unset: pairs for K < 32768 and the
+// epilogues in MMB_GEMM_PAIR_EPI_MASK (bit e = GemmEpilogue e), except the residual
+// epilogue at K <= 1024.  The default mask leaves out GELU and GELU-backward.
+// Measured on B200 (GPT-125M shapes, CUDA events): the two CTAs of a pair release
+// their accumulator together, so a pair runs at the pace of its slower epilogue, and
+// where the epilogue is heavy against a short main loop one CTA per tile is faster
+// (fc1 + GELU 90 against 96 us, fc2 dgrad + GELU-backward 74 against 80 us,
+// attn-out + residual at K = 768 39 against 41 us); elsewhere pairs are faster
+// (fc2 + residual at K = 3072 70 against 77 us, weight gradients 57 against 64 us),
+// except for the vocabulary-long K of the lm_head input gradient.
 int gemm_pairs_default(int K, int epi) {
   static const int mode = [] {
     const char* e = getenv("MMB_GEMM_PAIRS");
@@ -922,10 +929,13 @@ int gemm_pairs_default(int K, int epi) {
   }();
   static const unsigned mask = [] {
     const char* e = getenv("MMB_GEMM_PAIR_EPI_MASK");
-    return (e != nullptr && e[0] != 0) ? (unsigned)strtoul(e, nullptr, 0) : 0x1FFu;
+    return (e != nullptr && e[0] != 0) ? (unsigned)strtoul(e, nullptr, 0)
+                                       : 0x1FFu & ~((1u << EPI_GELU) | (1u << EPI_DGELU));
   }();
   if (mode >= 0) return mode == 1 ? 2 : 1;
-  return (K < 32768 && ((mask >> epi) & 1u)) ? 2 : 1;
+  if (K >= 32768 || !((mask >> epi) & 1u)) return 1;
+  if (epi == EPI_RESID && K <= 1024) return 1;
+  return 2;
 }
 
 }  // namespace mmb

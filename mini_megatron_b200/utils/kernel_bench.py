@@ -3,6 +3,7 @@
 Usage::
 
     python -m mini_megatron_b200.utils.kernel_bench gemm [--model gpt-125m] [--tokens 16384] [--pairs]
+    python -m mini_megatron_b200.utils.kernel_bench epi       # every fused GEMM epilogue, pairs vs one CTA
     python -m mini_megatron_b200.utils.kernel_bench attn      # causal attention vs torch SDPA
     python -m mini_megatron_b200.utils.kernel_bench attn_case --d 64   # one fwd + bwd launch (ncu target)
 
@@ -78,6 +79,40 @@ def bench_gemm(args):
             rec["pair_tflops"] = round(flops / t2 / 1e9, 1)
             rec["pair_vs_cta1_max_abs_diff"] = float((D.float() - D1.float()).abs().max())
         print(json.dumps(rec), flush=True)
+    assert _C.get_error() == 0
+
+
+def bench_epilogues(args):
+    """Every fused GEMM epilogue of a GPT-125M layer step, CUDA-event timed, with CTA pairs
+    (the default for these shapes) and with one CTA per tile (cg=1)."""
+    from mini_megatron_b200 import _C
+    torch.manual_seed(0)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+    T, H, F = args.tokens, 768, 3072
+    bf = dict(device="cuda", dtype=torch.bfloat16)
+    x, act, dy = torch.randn(T, H, **bf), torch.randn(T, F, **bf), torch.randn(T, H, **bf)
+    w1, w2, wo = (torch.randn(F, H, **bf) * 0.02, torch.randn(H, F, **bf) * 0.02, torch.randn(H, H, **bf) * 0.02)
+    wqkv, dqkv = torch.randn(3 * H, H, **bf) * 0.02, torch.randn(T, 3 * H, **bf)
+    out_f, gp, dpre = torch.empty(T, F, **bf), torch.empty(T, F, **bf), torch.empty(T, F, **bf)
+    resid, dx = torch.randn(T, H, device="cuda"), torch.empty(T, H, **bf)
+    dw1 = torch.zeros(F, H, device="cuda")
+    cases = [
+        ("fc1.fwd+gelu", 2 * T * F * H, lambda cg: _C.gemm(x, False, w1, False, out_f, _C.EPI_GELU, aux=gp, cg=cg)),
+        ("o.fwd+resid", 2 * T * H * H, lambda cg: _C.gemm(x, False, wo, False, resid, _C.EPI_RESID, resid=resid, cg=cg)),
+        ("fc2.fwd+resid", 2 * T * H * F, lambda cg: _C.gemm(act, False, w2, False, resid, _C.EPI_RESID, resid=resid,
+                                                           cg=cg)),
+        ("fc2.dgrad+dgelu", 2 * T * F * H, lambda cg: _C.gemm(dy, False, w2, True, dpre, _C.EPI_DGELU, aux=gp, cg=cg)),
+        ("qkv.dgrad", 2 * T * H * 3 * H, lambda cg: _C.gemm(dqkv, False, wqkv, True, dx, _C.EPI_BF16, cg=cg)),
+        ("fc1.wgrad+acc", 2 * T * F * H, lambda cg: _C.gemm(dpre, True, x, True, dw1, _C.EPI_F32_ACC, cg=cg)),
+    ]
+    for name, flops, fn in cases:
+        rec = {"kernel": "gemm_bf16_sm100", "case": name, "tokens": T}
+        for cg, key in ((0, "default"), (1, "cta1"), (2, "pair")):
+            ms = _timeit(lambda: fn(cg), flush=flush)
+            rec[key + "_us"] = round(ms * 1e3, 1)
+            rec[key + "_tflops"] = round(flops / ms / 1e9, 1)
+        print(json.dumps(rec), flush=True)
+    torch.cuda.synchronize()
     assert _C.get_error() == 0
 
 
@@ -209,7 +244,7 @@ def profile_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["gemm", "profile", "attn", "attn_case"])
+    ap.add_argument("kernel", choices=["gemm", "epi", "profile", "attn", "attn_case"])
     ap.add_argument("--model", default="gpt-125m")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--d", type=int, default=64)
@@ -217,7 +252,8 @@ def main():
     ap.add_argument("--pairs", action="store_true",
                     help="gemm: also time one CTA per 128x256 tile against a CTA pair per 256x256 tile")
     args = ap.parse_args()
-    {"gemm": bench_gemm, "profile": profile_case, "attn": bench_attn, "attn_case": attn_case}[args.kernel](args)
+    {"gemm": bench_gemm, "epi": bench_epilogues, "profile": profile_case, "attn": bench_attn,
+     "attn_case": attn_case}[args.kernel](args)
 
 
 if __name__ == "__main__":
