@@ -36,6 +36,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <unordered_map>
 
 namespace mmb {
 
@@ -679,21 +680,68 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
+// Encoded tensor maps, cached per host thread.  A map is a pure function of its
+// parameters (address, shape, leading dimension, box, element type), so a hit can be
+// reused whatever the memory holds now; the eager (un-captured) training step launches
+// the same few hundred GEMM / attention shapes on the same buffers every step.
+struct TmapKey {
+  const void* base;
+  long rows, cols, ld;
+  int box_cols, box_rows, dt;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && box_cols == o.box_cols &&
+           box_rows == o.box_rows && dt == o.dt;
+  }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+    for (uint64_t v : {(uint64_t)k.rows, (uint64_t)k.cols, (uint64_t)k.ld,
+                       ((uint64_t)k.box_cols << 32) | (uint32_t)k.box_rows, (uint64_t)k.dt})
+      h = (h ^ v) * 0x100000001B3ull;
+    return (size_t)(h ^ (h >> 29));
+  }
+};
+constexpr size_t kTmapCacheMax = 4096;  // cleared when full (a step uses far fewer)
+
+static bool tmap_cache_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("MMB_TMAP_CACHE");
+    return e == nullptr || e[0] != '0';
+  }();
+  return on;
+}
+
 // 2-D tensor map over a row-major matrix [rows, cols] with leading dimension
 // `ld` (elements), 128-byte swizzle, box {box_cols, box_rows}.
 static int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base, long rows, long cols,
                         long ld, int box_cols, int box_rows) {
-  PFN_encodeTiled enc = get_encode_fn();
-  if (!enc) return -1;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return -2;
   if ((ld * esize) % 16 != 0) return -3;
+  thread_local std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> cache;
+  const TmapKey key{base, rows, cols, ld, box_cols, box_rows, (int)dt};
+  const bool use_cache = tmap_cache_enabled();
+  if (use_cache) {
+    const auto it = cache.find(key);
+    if (it != cache.end()) {
+      *map = it->second;
+      return 0;
+    }
+  }
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return -1;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * esize)};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : -4;
+  if (r != CUDA_SUCCESS) return -4;
+  if (use_cache) {
+    if (cache.size() >= kTmapCacheMax) cache.clear();
+    cache.emplace(key, *map);
+  }
+  return 0;
 }
 
 int make_tmap_bf16_2d(CUtensorMap* map, const void* base, long rows, long cols, long ld, int box_cols,
