@@ -30,6 +30,7 @@
 // for the same MMA work.
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "gemm_tiles.h"
 #include "peer.cuh"
 
 #include <algorithm>
@@ -42,6 +43,7 @@ namespace mmb {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+static_assert(BM == tiles::kBM, "tile mapping and kernel disagree on the m-tile height");
 constexpr int kGemmThreads = 320;  // 2 producer/MMA warps + 8 epilogue warps
 constexpr int kEpiWarps = 8;
 
@@ -58,48 +60,12 @@ struct GemmCfg {
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 8 * 4096 /*epilogue*/ + 256;  // one 4 KB stage per epilogue warp
 };
 
-// Grouped rasterisation: walk GROUP_M m-tiles down each n column so the B
-// tile and a band of A tiles stay hot in L2.
-__device__ __forceinline__ void tile_coords(int t, int mtiles, int ntiles, int& tm, int& tn) {
-  constexpr int GROUP_M = 16;
-  const int per_group = GROUP_M * ntiles;
-  const int g = t / per_group;
-  const int first_m = g * GROUP_M;
-  const int gsz = min(mtiles - first_m, GROUP_M);
-  const int r = t - g * per_group;
-  tm = first_m + r % gsz;
-  tn = r / gsz;
-}
-
-// Tile order of a GEMM.  For an all-gather consumer the 128-row tiles of each
-// sequence are rotated by this rank's shard (rank * Sl rows), so every rank
-// starts with the rows it produced itself (already local) while the peers'
-// shards are still arriving.
-__device__ __forceinline__ int ag_rotate(const GemmArgs& args, int tm) {
-  const int tps = args.ag_S / BM;
-  const int b = tm / tps, k = tm % tps;
-  return b * tps + (k + args.ag_rank * (args.ag_Sl / BM)) % tps;
-}
-__device__ __forceinline__ void gemm_tile(const GemmArgs& args, int t, int mtiles, int ntiles, int& tm, int& tn) {
-  tile_coords(t, mtiles, ntiles, tm, tn);
-  if (args.ag_flags != nullptr) tm = ag_rotate(args, tm);
-}
-
-// This CTA's 128-row m-tile and BN-wide n-tile of work unit u (u / splits is the
-// output tile; for a CTA pair, the output tile is a pair of m-tiles 2p, 2p + 1 that
-// share one n-tile, and CTA `crank` of the pair takes m-tile 2p + crank).  The
-// rotation of an all-gather consumer is applied per 128-row m-tile: the pair MMA
-// needs the two CTAs to share B, not to hold adjacent rows of A.
+// Work-unit -> tile mapping (gemm_tiles.h), with the all-gather parameters of the launch.
 template <int CG>
 __device__ __forceinline__ void unit_tile(const GemmArgs& args, int u, int splits, int mtiles, int ntiles, int crank,
                                           int& tm, int& tn) {
-  if constexpr (CG == 1) {
-    gemm_tile(args, u / splits, mtiles, ntiles, tm, tn);
-  } else {
-    tile_coords(u / splits, (mtiles + 1) >> 1, ntiles, tm, tn);
-    tm = 2 * tm + crank;
-    if (args.ag_flags != nullptr && tm < mtiles) tm = ag_rotate(args, tm);
-  }
+  tiles::unit_tile<CG>(u, splits, mtiles, ntiles, crank, args.ag_flags != nullptr, args.ag_S, args.ag_Sl,
+                       args.ag_rank, tm, tn);
 }
 
 // ---------------------------------------------------------------- epilogue helpers
@@ -230,7 +196,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Work unit = (output tile, K split).  Splits > 1 only with the atomic epilogue.
   const int splits = args.splits > 0 ? args.splits : 1;
   const int kb_per_split = (kblocks_total + splits - 1) / splits;
-  const int num_tiles = (CG == 1 ? mtiles : (mtiles + 1) >> 1) * ntiles * splits;
+  const int num_tiles = tiles::num_units(mtiles, ntiles, splits, CG);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
